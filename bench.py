@@ -1,0 +1,344 @@
+"""Benchmark of the Polar Switch hot path on B200.
+
+Default workload: the Qwen3-0.6B-shaped Muon orthogonalization step (BASELINE
+config 4): 196 matrices (28 layers x q 2048x1024, k/v 1024x1024, o 1024x2048,
+gate/up 3072x1024, down 1024x3072), N(0,1) fp32 from a fixed seed, method
+PS2_55, sharded by FLOPs across the ranks with one NCCL all-gather of the FP16
+updates. A step is one pass over all 196 matrices. `value` is the algorithmic
+TFLOP/s of the whole job (PS2-55 FLOPs (6a+10)n^3 per matrix over the step
+time, max over ranks).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload qwen|gemma|nanogpt|single]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference ...     # the reference's CPU path, timed on host cores
+
+Prints one JSON line (rank 0).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "polar-switch_b200"))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+WORKLOADS = {
+    "qwen": dict(desc="Qwen3-0.6B Muon step (BASELINE config 4)", method="PS2_55"),
+    "gemma": dict(desc="Gemma-3-1B Muon step (BASELINE config 5)", method="PS3_55"),
+    "nanogpt": dict(desc="Modded-NanoGPT Muon batch (BASELINE config 3)", method="PS3_55"),
+    "single": dict(desc="single 8192x8192 matrix (BASELINE config 2, published heatmap point)",
+                   method="PS2_55"),
+}
+
+
+def bank_shapes(workload):
+    from polar_switch import distributed as pd
+    if workload == "qwen":
+        return pd.qwen3_0_6b_banks()
+    if workload == "gemma":
+        return pd.gemma3_1b_banks()
+    if workload == "nanogpt":
+        return pd.nanogpt_banks()
+    if workload == "single":
+        return [(1, 8192, 8192)]
+    raise ValueError(workload)
+
+
+def make_banks(shapes, device, seed=0, scale=1.0):
+    """Seeded N(0, scale^2) fp32 banks, generated on the device (deterministic per seed)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return [torch.randn(L, r, c, generator=g, device=device, dtype=torch.float32) * scale
+            for L, r, c in shapes]
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([v.strip() for v in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        smax = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(value, world, device):
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_reference_sample(shapes, method, budget_s=12.0, max_layers=None):
+    """Time the reference CPU path (a port: POLAR_EXPRESS via torch.bmm/baddbmm on
+    FP16, reference polar_switch/__init__.py:48-63,180-182) on a bounded sample:
+    whole layers (one matrix of each bank per layer), repeated until `budget_s`.
+    Returns (seconds per full workload step extrapolated, sample description)."""
+    sys.path.insert(0, ROOT)
+    from oracle.reference_cpu import torch_pe
+    from polar_switch import circuit_flops, coefficients
+    layers = min(L for L, _, _ in shapes)
+    per_layer = [(max(1, L // layers), r, c) for L, r, c in shapes]
+    g = torch.Generator().manual_seed(1)
+    mats = [torch.randn(k, r, c, generator=g) for k, r, c in per_layer]
+    torch_pe(mats[0][:1, :64, :64])  # warm-up of the thread pool
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for M in mats:
+            torch_pe(M)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_layers and reps >= max_layers):
+            break
+    per_layer_s = el / reps
+    step_s = per_layer_s * layers
+    desc = (f"{reps} layer(s) of {sum(k for k, _, _ in per_layer)} matrices "
+            f"({', '.join(f'{k}x{r}x{c}' for k, r, c in per_layer)}), {el:.1f} s, "
+            f"extrapolated x{layers} layers; reference CPU path = POLAR_EXPRESS in torch FP16 bmm "
+            f"(requested {method}); FLOPs counted as the requested {method} circuit")
+    return step_s, desc
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference CPU implementation on the host cores."""
+    if rank != 0:
+        return
+    shapes = bank_shapes(args.workload)
+    method = WORKLOADS[args.workload]["method"]
+    from polar_switch import circuit_flops, coefficients
+    table = getattr(coefficients, method)
+    flops = sum(L * circuit_flops(table, r, c) for L, r, c in shapes)
+    threads = torch.get_num_threads()
+    times = []
+    for i in range(args.warmup + args.steps):
+        s, desc = cpu_reference_sample(shapes, method, budget_s=args.ref_budget, max_layers=1)
+        if i >= args.warmup:
+            times.append(s)
+    step_s = statistics.median(times)
+    value = flops / step_s / 1e12
+    line = {
+        "impl": "reference", "metric": "muon_step_orthogonalize_tflops" if args.workload != "single"
+        else "orthogonalize_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": config_dict(args, shapes, method),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, shapes, method):
+    total = sum(L for L, _, _ in shapes)
+    in_bytes = sum(L * r * c * 4 for L, r, c in shapes)
+    return {"workload": f"{args.workload}: {WORKLOADS[args.workload]['desc']}", "method": method,
+            "matrices": total, "banks": [list(s) for s in shapes], "input": "fp32 N(0,1), seed 0",
+            "l2": f"inputs larger than L2 ({in_bytes / 1e9:.2f} GB per step vs 126 MB L2)",
+            "parallelism": f"matrix-sharded x{args.gpus}, NCCL all-gather of FP16 updates"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="qwen", choices=sorted(WORKLOADS))
+    ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    from polar_switch import _native as nat
+    from polar_switch.distributed import ShardedOrthogonalizer
+
+    shapes = bank_shapes(args.workload)
+    method = WORKLOADS[args.workload]["method"]
+    banks = make_banks(shapes, device, seed=0)
+    step = ShardedOrthogonalizer(shapes, method=method, group=None, device=device,
+                                 world_size=world, rank=rank)
+    flops = step.flops_total
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        step(banks)
+    barrier()
+
+    stream = torch.cuda.current_stream(device)
+    t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = nat.launch_count()
+    with ClockSampler(local) as clocks:
+        barrier()
+        t_start.record(stream)
+        for _ in range(args.steps):
+            step(banks)
+        t_stop.record(stream)
+        barrier()
+    launches = nat.launch_count() - launches0
+    ms = t_start.elapsed_time(t_stop) / args.steps
+    ms = max_over_ranks(ms, world, device)
+    value = flops / (ms * 1e-3) / 1e12
+
+    # Per-kernel-class device time from CUDA events around each launch, over
+    # a second pass of the same steps (kept out of the headline timing).
+    nat.profile_enable(True)
+    barrier()
+    for _ in range(args.steps):
+        step(banks)
+    barrier()
+    prof = nat.profile_read()
+    nat.profile_enable(False)
+
+    # End-to-end through the public API with host buffers: each rank uploads
+    # its own slices from pinned memory, runs the step, and downloads the full
+    # gathered FP16 update set.
+    host_banks = [b.cpu().pin_memory() for b in banks]
+    host_out = torch.empty(step.recv.numel(), dtype=torch.float16).pin_memory()
+    h2d = 0
+    for rank_slice, (L, r, c) in zip(step.slices[rank], shapes):
+        h2d += rank_slice[1] * r * c * 4
+    dev_banks = [torch.empty_like(b) for b in banks]
+
+    def e2e_step():
+        for hb, db, (start, count) in zip(host_banks, dev_banks, step.slices[rank]):
+            if count:
+                db[start:start + count].copy_(hb[start:start + count], non_blocking=True)
+        out = step(dev_banks)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e_stop.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.e2e_steps, world, device)
+    d2h = host_out.numel() * 2
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        step_s, desc = cpu_reference_sample(shapes, method, budget_s=args.ref_budget)
+        cpu_baseline = {"value": flops / step_s / 1e12, "unit": "TFLOP/s",
+                        "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
+
+    if rank == 0:
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        gemm_kinds = {k: v for k, v in prof.items() if k in ("gram", "square", "apply") and v["launches"]}
+        dom_name, dom = max(gemm_kinds.items(), key=lambda kv: kv[1]["ms"])
+        achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained")
+        peak_src = "measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
+        if peak is None:
+            peak, peak_src = 1400.0, "fallback sustained"
+        breakdown = {k: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
+                         "tflops": (v["flops"] / (v["ms"] * 1e-3) / 1e12) if v["ms"] and v["flops"] else None,
+                         "gbs": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) if v["ms"] else None}
+                     for k, v in prof.items() if v["launches"]}
+        line = {
+            "metric": "muon_step_orthogonalize_tflops" if args.workload != "single" else "orthogonalize_tflops",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": config_dict(args, shapes, method),
+            "roofline": {"bound": "tensor", "kernel": f"ps_gemm ({dom_name})", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": peak_src, "traffic": None,
+                         "launches_per_step": dom["launches"] / args.steps},
+            "kernels": breakdown,
+            "cpu_baseline": cpu_baseline,
+            "clocks": clocks.summary(),
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+        }
+        if args.workload == "single":
+            line["vs_baseline"] = value / 1177.0  # published 7.47 ms for 8192^2 PS2-55
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+/*
+ * polar_switch_b200 -- C ABI of the B200 (sm_100a) Polar Switch orthogonalizer.
+ *
+ * Every entry point takes plain device pointers, sizes, FP32 scalars and a
+ * cudaStream_t passed as `void*` (NULL = legacy default stream). All work is
+ * enqueued on that stream; no entry point synchronises the host except
+ * ps_get_status(). The library allocates no device memory: the caller owns
+ * every buffer, including the scratch `workspace` of ps_normalize/ps_circuit.
+ *
+ * Return value: PS_OK (0) or a negative PS_ERR_* code; ps_last_error()
+ * returns a message for the calling thread's last failure.
+ *
+ * FP16 matrices passed to gram/square/sym_product/apply are row-major with a
+ * row pitch (`*_ld`, in elements) that is a multiple of 8, on 16-byte aligned
+ * addresses; batch `l` starts at `ptr + l * rows * ld`.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   polar_switch/__init__.py:25-45          _run                -> ps_circuit
+ *   polar_switch/__init__.py:34-35          FP32 normalise      -> ps_normalize
+ *   polar_switch/gemm_symmetric_fused.py:291-293 / triton_kernels.py:72-74
+ *                                           gram(X, tall, out)  -> ps_gram
+ *   polar_switch/gemm_symmetric_fused.py:296-301 / triton_kernels.py:77-79
+ *                                           square(A, C, out, alpha, beta, diag) -> ps_square
+ *   polar_switch/gram_newton_schulz.py:64-72 sym_baddbmm(A, B, C, alpha, beta)   -> ps_sym_product
+ *   polar_switch/gemm_symmetric_fused.py:304-309 / triton_kernels.py:82-87
+ *                                           apply(X, B, tall, residual) -> ps_apply
+ *   polar_switch/gram_newton_schulz.py:107  Q = Z + a*I          -> ps_add_diag
+ */
+#ifndef POLAR_SWITCH_B200_H
+#define POLAR_SWITCH_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PS_API __attribute__((visibility("default")))
+#else
+#define PS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PS_OK 0
+#define PS_ERR_INVALID (-1)     /* bad argument (null pointer, size, alignment, table) */
+#define PS_ERR_CUDA (-2)        /* a CUDA runtime/driver call failed */
+#define PS_ERR_UNSUPPORTED (-3) /* device or shape outside what the kernels support */
+#define PS_ERR_WORKSPACE (-4)   /* workspace smaller than ps_*_workspace_bytes() */
+
+/* dtype codes */
+#define PS_F16 0
+#define PS_F32 1
+#define PS_BF16 2
+#define PS_F64 3
+
+/* One inner iteration (w, i, r, a, b, c) of a coefficient table:
+ * B[dst] = alpha * B[src] @ B[src] + beta * B[add] + diag * I
+ * (polar_switch/coefficients.py:1-8). */
+typedef struct ps_step {
+  int32_t dst, src, add;
+  float alpha, beta, diag;
+} ps_step;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+PS_API int ps_version(void);
+
+/* Message describing the calling thread's last error ("" if none). */
+PS_API const char* ps_last_error(void);
+
+/* Device status word of the current device: 0, or the code of the first
+ * bounded wait inside a kernel that ran out (the kernel then returned early
+ * and its output is undefined). Synchronous; `clear` resets it to 0. */
+PS_API int ps_get_status(int* status, int clear);
+
+/* Upper bound, in SM clock cycles, for every spin-wait inside the kernels
+ * launched afterwards by this process (default 2^32, about two seconds). */
+PS_API int ps_set_wait_limit(long long cycles);
+
+/* Number of kernels this library has launched in the process so far. */
+PS_API long long ps_launch_count(void);
+
+/* Profiling of the library's own launches: enable=1 clears the records and
+ * brackets every later launch with CUDA events on its stream; enable=0 stops
+ * recording. ps_profile_read waits for the recorded launches of one class
+ * (0 normalise, 1 gram, 2 square/symmetric product, 3 apply, 4 other) and
+ * returns their summed device time, count, algorithmic FLOPs and algorithmic
+ * HBM bytes. */
+PS_API int ps_profile_enable(int enable);
+PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double* flops,
+                           double* bytes);
+
+/* Launches one kernel whose single wait can never be satisfied, so that it
+ * runs out after `limit_cycles` and records its status code (5). Used by the
+ * tests of the bounded-wait path. */
+PS_API int ps_selftest_wait(long long limit_cycles, void* stream);
+
+/* Scratch bytes ps_normalize needs for L matrices of rows x cols. */
+PS_API int64_t ps_normalize_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
+
+/* xh[l] = fp16( fp32(x[l]) / (||fp32(x[l])||_F + eps) ), per matrix.
+ * x: (L, rows, cols) of x_dtype with element strides (sL, sR, sC).
+ * xh: FP16 (L, rows_p, cols_p) contiguous with rows_p >= rows, cols_p >= cols;
+ * the padding is written with zeros. Replaces polar_switch/__init__.py:34-35. */
+PS_API int ps_normalize(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                 int64_t sR, int64_t sC, float eps, void* xh, int64_t rows_p, int64_t cols_p,
+                 void* workspace, int64_t workspace_bytes, void* stream);
+
+/* out = x @ x^T (rows <= cols) or x^T @ x (rows > cols), FP32 accumulate,
+ * one FP16 rounding; out is (L, n, n) contiguous, n = min(rows, cols), n % 8 == 0.
+ * Replaces gram() of polar_switch/gemm_symmetric_fused.py:291-293. */
+PS_API int ps_gram(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
+            void* stream);
+
+/* out = fp16(alpha * a @ a + beta * c + diag * I) for symmetric a; out may be
+ * c but not a; c may be NULL (no addend). (L, n, n) contiguous, n % 8 == 0.
+ * Replaces square() of polar_switch/gemm_symmetric_fused.py:296-301. */
+PS_API int ps_square(const void* a, const void* c, void* out, int64_t L, int64_t n, float alpha,
+              float beta, float diag, void* stream);
+
+/* out = fp16(alpha * p @ q + beta * c + diag * I) for symmetric, commuting p
+ * and q (so the product is symmetric; only one triangle is computed and
+ * mirrored); out may be c but neither p nor q; c may be NULL.
+ * Replaces sym_baddbmm of polar_switch/gram_newton_schulz.py:64-72. */
+PS_API int ps_sym_product(const void* p, const void* q, const void* c, void* out, int64_t L, int64_t n,
+                   float alpha, float beta, float diag, void* stream);
+
+/* y = b @ x + residual * x (rows <= cols) or x @ b + residual * x (rows > cols),
+ * FP32 accumulate, one FP16 rounding, stored as y_dtype (PS_F16, PS_F32 or
+ * PS_BF16; wider types are the FP16 value widened). b: (L, n, n) contiguous
+ * symmetric; x: (L, rows, cols) FP16 with pitch x_ld; y: pitch y_ld elements
+ * (y_ld * sizeof(y_dtype) % 16 == 0). y must not overlap x or b.
+ * Replaces apply() of polar_switch/gemm_symmetric_fused.py:304-309. */
+PS_API int ps_apply(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
+             int64_t x_ld, float residual, int y_dtype, int64_t y_ld, void* stream);
+
+/* out = fp16(in + fp16(a) * I), (L, n, n) contiguous; out may equal in.
+ * Replaces `Z + a * I` of polar_switch/gram_newton_schulz.py:107. */
+PS_API int ps_add_diag(const void* in, void* out, int64_t L, int64_t n, float a, void* stream);
+
+/* Scratch bytes ps_circuit needs for L matrices of rows x cols and `buffers`
+ * square buffers. */
+PS_API int64_t ps_circuit_workspace_bytes(int64_t L, int64_t rows, int64_t cols, int buffers);
+
+/* Whole Polar Switch circuit (polar_switch/__init__.py:25-45 plus the output
+ * cast of :168): normalise x, then for each outer iteration t
+ *   B[0] = gram(X); for each step: B[w] = a B[i]@B[i] + b B[r] + c I;
+ *   X = B[w_last] @ X + residual_t X   (X @ B[w_last] + ... for rows > cols)
+ * and write y (L, rows, cols) contiguous in y_dtype (any PS_* code).
+ * x: (L, rows, cols) of x_dtype with element strides (sL, sR, sC).
+ * Table: n_outer outer iterations; outer t has n_steps[t] consecutive entries
+ * of `steps`; `buffers` square buffers. Validated like
+ * polar_switch/__init__.py:107-122 (PS_ERR_INVALID on a bad table). */
+PS_API int ps_circuit(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+               int64_t sR, int64_t sC, void* y, int y_dtype, int n_outer,
+               const float* residuals, const int32_t* n_steps, const ps_step* steps, int buffers,
+               float eps, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* One problem of a grouped circuit: x (L, rows, cols) of x_dtype with element
+ * strides (sL, sR, sC); y (L, rows, cols) contiguous of y_dtype. */
+typedef struct ps_problem {
+  const void* x;
+  int32_t x_dtype;
+  int64_t L, rows, cols, sL, sR, sC;
+  void* y;
+  int32_t y_dtype;
+} ps_problem;
+
+/* Scratch bytes ps_circuit_grouped needs for these problems. */
+PS_API int64_t ps_circuit_grouped_workspace_bytes(const ps_problem* probs, int n_probs, int buffers);
+
+/* The circuit of ps_circuit applied to several problems of different shapes
+ * (the buckets of a Muon step, reference training/muon.py:59-86), in one call:
+ * the inner iterations of all problems that share n = min(rows, cols) run as
+ * one batched launch per inner iteration. Same table and errors as ps_circuit. */
+PS_API int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer,
+                              const float* residuals, const int32_t* n_steps, const ps_step* steps,
+                              int buffers, float eps, void* workspace, int64_t workspace_bytes,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POLAR_SWITCH_B200_H */

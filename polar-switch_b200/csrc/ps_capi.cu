@@ -1,0 +1,874 @@
+// C-ABI entry points of libpolarswitch_b200.so: argument validation, TMA
+// tensor-map encoding, launch configuration and the circuit driver. One
+// translation unit holds all device code so the status word is a single
+// module-scope symbol.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/polar_switch_b200.h"
+#include "ps_gemm.cuh"
+#include "ps_norm.cuh"
+
+namespace ps {
+// First error code recorded by a bounded wait in any kernel on this device.
+__device__ int g_status;
+}  // namespace ps
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxDevices = 64;
+constexpr int kNumVariants = 16;
+
+// Launch classes reported by ps_profile_read.
+enum ProfKind : int {
+  kProfNormalize = 0,
+  kProfGram = 1,
+  kProfSquare = 2,
+  kProfApply = 3,
+  kProfOther = 4,
+  kNumProfKinds = 5
+};
+
+thread_local std::string g_last_error;
+long long g_wait_limit = ps::kDefaultWaitLimit;
+
+// Every kernel launch of the library is counted; when profiling is enabled,
+// each launch is also bracketed by CUDA events on its stream and tagged with
+// its algorithmic FLOPs and bytes.
+std::atomic<long long> g_launches{0};
+
+struct ProfRecord {
+  int kind;
+  cudaEvent_t start, stop;
+  double flops, bytes;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pooled_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+class LaunchScope {
+ public:
+  LaunchScope(int kind, cudaStream_t s, double flops, double bytes) : s_(s) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    std::lock_guard<std::mutex> lock(g_prof_mu);
+    if (!g_prof_on) return;
+    rec_.kind = kind;
+    rec_.flops = flops;
+    rec_.bytes = bytes;
+    rec_.start = pooled_event();
+    rec_.stop = pooled_event();
+    active_ = rec_.start && rec_.stop && cudaEventRecord(rec_.start, s_) == cudaSuccess;
+  }
+  ~LaunchScope() {
+    if (!active_) return;
+    if (cudaEventRecord(rec_.stop, s_) != cudaSuccess) return;
+    std::lock_guard<std::mutex> lock(g_prof_mu);
+    g_prof.push_back(rec_);
+  }
+
+ private:
+  cudaStream_t s_;
+  ProfRecord rec_{};
+  bool active_ = false;
+};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+struct DeviceState {
+  bool ready = false;
+  int sms = 0;
+  int* status = nullptr;  // device address of ps::g_status on this device
+  bool smem_attr[kNumVariants] = {};
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+
+// Per-device set-up, done with that device current: SM count, capability
+// check and the device address of the status word.
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PS_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.ready) {
+    int major = 0, minor = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    if ((e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (major != 10 || minor != 0)
+      return fail(PS_ERR_UNSUPPORTED,
+                  "polar_switch_b200 kernels are built for sm_100a (B200); device %d is sm_%d%d",
+                  dev, major, minor);
+    if ((e = cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, ps::g_status)) != cudaSuccess)
+      return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    st.status = static_cast<int*>(p);
+    st.ready = true;
+  }
+  *out = &st;
+  return PS_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int elem_bytes(int dtype) {
+  switch (dtype) {
+    case PS_F16:
+    case PS_BF16:
+      return 2;
+    case PS_F32:
+      return 4;
+    case PS_F64:
+      return 8;
+    default:
+      return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 3-D tiled tensor map over (cols, rows, L) of a row-major batched matrix.
+int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t cols, int64_t rows, int64_t L,
+             int64_t ld, int64_t bs, uint32_t box_cols, uint32_t box_rows,
+             CUtensorMapSwizzle swizzle) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const int eb = elem_bytes(dtype);
+  CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (dtype == PS_F32) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  if (dtype == PS_BF16) dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(L)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * eb), static_cast<cuuint64_t>(bs * eb)};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PS_ERR_INVALID,
+                "cuTensorMapEncodeTiled failed (%d): cols=%lld rows=%lld L=%lld ld=%lld bs=%lld",
+                static_cast<int>(r), (long long)cols, (long long)rows, (long long)L,
+                (long long)ld, (long long)bs);
+  return PS_OK;
+}
+
+// Operand maps: K-major tiles are (64 K) x (rows), MN-major tiles are boxes of
+// (64 M/N) x (64 K); both with 128-byte swizzle.
+int map_kmajor(CUtensorMap* m, const void* p, int64_t k, int64_t mn, int64_t L, int64_t ld,
+               int64_t bs, uint32_t rows_box) {
+  return make_map(m, p, PS_F16, k, mn, L, ld, bs, 64, rows_box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+int map_mnmajor(CUtensorMap* m, const void* p, int64_t mn, int64_t k, int64_t L, int64_t ld,
+                int64_t bs) {
+  return make_map(m, p, PS_F16, mn, k, L, ld, bs, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+// Output map: 32 x 32 sub-tiles, swizzle matching the epilogue's staging.
+int map_out(CUtensorMap* m, const void* p, int dtype, int64_t cols, int64_t rows, int64_t L,
+            int64_t ld, int64_t bs) {
+  const CUtensorMapSwizzle sw =
+      elem_bytes(dtype) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return make_map(m, p, dtype, cols, rows, L, ld, bs, 32, 32, sw);
+}
+
+template <bool A_MN, bool B_MN, bool SYM, int OUT>
+int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                ps::GemmArgs args, cudaStream_t stream, int kind, double flops, double bytes) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  auto kern = ps::ps_gemm_kernel<A_MN, B_MN, SYM, OUT>;
+  if (!st->smem_attr[variant]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, ps::SMEM_TOTAL);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm smem)");
+    st->smem_attr[variant] = true;
+  }
+  if (args.total_tiles <= 0) return PS_OK;
+  args.status = st->status;
+  args.wait_limit = g_wait_limit;
+  const int grid = args.total_tiles < st->sms ? args.total_tiles : st->sms;
+  LaunchScope scope(kind, stream, flops, bytes);
+  kern<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(ta, tb, td, args);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return PS_OK;
+}
+
+void fill_sym_tiles(ps::GemmArgs& a, int64_t n, int64_t L) {
+  a.tb = static_cast<int>((n + ps::BM - 1) / ps::BM);
+  int per = 0;
+  for (int bi = 0; bi < a.tb; ++bi) per += (a.tb - bi + 1) / 2;
+  a.tiles_per_mat = per;
+  a.total_tiles = static_cast<int>(L * per);
+  a.tiles_m = a.tiles_n = 0;
+  a.group_m = 1;
+}
+
+void fill_gen_tiles(ps::GemmArgs& a, int64_t M, int64_t N, int64_t L) {
+  a.tiles_m = static_cast<int>((M + ps::BM - 1) / ps::BM);
+  a.tiles_n = static_cast<int>((N + ps::BN - 1) / ps::BN);
+  a.group_m = a.tiles_m < 16 ? a.tiles_m : 16;
+  a.tiles_per_mat = a.tiles_m * a.tiles_n;
+  a.total_tiles = static_cast<int>(L * a.tiles_per_mat);
+  a.tb = 0;
+}
+
+ps::GemmArgs base_args(int64_t M, int64_t N, int64_t K, int64_t L) {
+  ps::GemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.L = static_cast<int>(L);
+  a.alpha = 1.f;
+  return a;
+}
+
+bool dims_ok(int64_t L, int64_t r, int64_t c) {
+  const int64_t lim = int64_t(1) << 30;
+  return L > 0 && r > 0 && c > 0 && L < lim && r < lim && c < lim && L * r * c < (int64_t(1) << 46);
+}
+
+// ------------------------------------------------------------------ ops
+int sym_product_impl(const void* p, const void* q, const void* c, void* out, int64_t L,
+                     int64_t n, float alpha, float beta, float diag, cudaStream_t stream,
+                     const char* name) {
+  if (!p || !q || !out) return fail(PS_ERR_INVALID, "%s: null pointer", name);
+  if (!dims_ok(L, n, n)) return fail(PS_ERR_INVALID, "%s: bad sizes", name);
+  if (n % 8) return fail(PS_ERR_INVALID, "%s: n=%lld must be a multiple of 8", name, (long long)n);
+  if (!aligned16(p) || !aligned16(q) || !aligned16(out) || (c && !aligned16(c)))
+    return fail(PS_ERR_INVALID, "%s: pointers must be 16-byte aligned", name);
+  if (out == p || out == q)
+    return fail(PS_ERR_INVALID, "%s: the output must not be a multiplied operand", name);
+  CUtensorMap ta, tb, td;
+  int rc;
+  if ((rc = map_kmajor(&ta, p, n, n, L, n, n * n, ps::BM))) return rc;
+  if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, ps::BN))) return rc;
+  if ((rc = map_out(&td, out, PS_F16, n, n, L, n, n * n))) return rc;
+  ps::GemmArgs a = base_args(n, n, n, L);
+  fill_sym_tiles(a, n, L);
+  a.alpha = alpha;
+  a.beta = beta;
+  a.diag = diag;
+  a.C = static_cast<const __half*>(c);
+  a.c_ld = n;
+  a.c_bs = n * n;
+  a.has_addend = c != nullptr;
+  a.has_diag = diag != 0.f;
+  const double nn = static_cast<double>(n) * n;
+  const double bytes = L * nn * 2.0 * ((p == q ? 1 : 2) + (c ? 1 : 0) + 1);
+  return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
+                                                      L * nn * n, bytes);
+}
+
+int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
+              bool tall, cudaStream_t stream) {
+  if (!x || !out) return fail(PS_ERR_INVALID, "ps_gram: null pointer");
+  if (!dims_ok(L, rows, cols) || x_ld < cols)
+    return fail(PS_ERR_INVALID, "ps_gram: bad sizes");
+  if (x_ld % 8) return fail(PS_ERR_INVALID, "ps_gram: x_ld must be a multiple of 8");
+  if (!aligned16(x) || !aligned16(out))
+    return fail(PS_ERR_INVALID, "ps_gram: pointers must be 16-byte aligned");
+  const int64_t n = tall ? cols : rows, K = tall ? rows : cols;
+  if (n % 8) return fail(PS_ERR_INVALID, "ps_gram: min(rows, cols) must be a multiple of 8");
+  CUtensorMap ta, tb, td;
+  int rc;
+  if ((rc = map_out(&td, out, PS_F16, n, n, L, n, n * n))) return rc;
+  ps::GemmArgs a = base_args(n, n, K, L);
+  fill_sym_tiles(a, n, L);
+  const double flops = static_cast<double>(L) * n * n * K;
+  const double bytes = static_cast<double>(L) * 2.0 * (static_cast<double>(n) * K + n * n);
+  if (!tall) {
+    if ((rc = map_kmajor(&ta, x, K, n, L, x_ld, rows * x_ld, ps::BM))) return rc;
+    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, ps::BN))) return rc;
+    return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfGram,
+                                                        flops, bytes);
+  }
+  if ((rc = map_mnmajor(&ta, x, n, K, L, x_ld, rows * x_ld))) return rc;
+  return launch_gemm<true, true, true, ps::kOutF16>(1, ta, ta, td, a, stream, kProfGram, flops,
+                                                    bytes);
+}
+
+template <int OUT>
+int apply_launch(bool tall, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                 const ps::GemmArgs& a, cudaStream_t s) {
+  const double M = a.M, N = a.N, K = a.K, L = a.L;
+  const double out_bytes = OUT == ps::kOutF32 ? 4.0 : 2.0;
+  const double flops = 2.0 * L * M * N * K;
+  const double bytes = L * (2.0 * K * K + 2.0 * M * N + out_bytes * M * N);
+  if (!tall) return launch_gemm<false, true, false, OUT>(2 + OUT, ta, tb, td, a, s, kProfApply,
+                                                         flops, bytes);
+  return launch_gemm<false, false, false, OUT>(5 + OUT, ta, tb, td, a, s, kProfApply, flops,
+                                               bytes);
+}
+
+int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
+               int64_t x_ld, float residual, int y_dtype, int64_t y_ld, bool tall,
+               cudaStream_t stream) {
+  if (!b || !x || !y) return fail(PS_ERR_INVALID, "ps_apply: null pointer");
+  if (!dims_ok(L, rows, cols) || x_ld < cols || y_ld < cols)
+    return fail(PS_ERR_INVALID, "ps_apply: bad sizes");
+  if (y_dtype != PS_F16 && y_dtype != PS_F32 && y_dtype != PS_BF16)
+    return fail(PS_ERR_INVALID, "ps_apply: y_dtype must be PS_F16, PS_F32 or PS_BF16");
+  if (x_ld % 8 || (y_ld * elem_bytes(y_dtype)) % 16)
+    return fail(PS_ERR_INVALID, "ps_apply: row pitches must be multiples of 16 bytes");
+  if (!aligned16(b) || !aligned16(x) || !aligned16(y))
+    return fail(PS_ERR_INVALID, "ps_apply: pointers must be 16-byte aligned");
+  if (y == x || y == b) return fail(PS_ERR_INVALID, "ps_apply: y must not alias x or b");
+  const int64_t n = tall ? cols : rows, m = tall ? rows : cols;
+  if (n % 8) return fail(PS_ERR_INVALID, "ps_apply: min(rows, cols) must be a multiple of 8");
+  CUtensorMap ta, tb, td;
+  int rc;
+  const int64_t M = tall ? m : n, N = tall ? n : m;
+  if ((rc = map_out(&td, y, y_dtype, N, M, L, y_ld, rows * y_ld))) return rc;
+  if (!tall) {
+    if ((rc = map_kmajor(&ta, b, n, n, L, n, n * n, ps::BM))) return rc;
+    if ((rc = map_mnmajor(&tb, x, m, n, L, x_ld, rows * x_ld))) return rc;
+  } else {
+    if ((rc = map_kmajor(&ta, x, n, m, L, x_ld, rows * x_ld, ps::BM))) return rc;
+    if ((rc = map_kmajor(&tb, b, n, n, L, n, n * n, ps::BN))) return rc;
+  }
+  ps::GemmArgs a = base_args(M, N, n, L);
+  fill_gen_tiles(a, M, N, L);
+  if (residual != 0.f) {
+    a.has_addend = 1;
+    a.beta = residual;
+    a.C = static_cast<const __half*>(x);
+    a.c_ld = x_ld;
+    a.c_bs = rows * x_ld;
+  }
+  switch (y_dtype) {
+    case PS_F16:
+      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream);
+    case PS_F32:
+      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream);
+    default:
+      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream);
+  }
+}
+
+// ------------------------------------------------------------------ normalise
+int norm_chunks(int64_t L, int64_t rows, int64_t cols, int sms) {
+  // Enough blocks in flight for HBM bandwidth: about 4 per SM in total.
+  const int64_t E = rows * cols;
+  int64_t want = (4LL * sms + L - 1) / L;
+  const int64_t max_by_size = (E + 4095) / 4096;  // at least 4096 elements per block
+  if (want > max_by_size) want = max_by_size;
+  if (want > rows) want = rows;  // strided path splits by rows
+  if (want < 1) want = 1;
+  if (want > 1024) want = 1024;
+  return static_cast<int>(want);
+}
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+template <typename T>
+int launch_normalize(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL, int64_t sR,
+                     int64_t sC, float eps, void* xh, int64_t Rp, int64_t Cp, double* partial,
+                     int chunks, int sms, cudaStream_t s) {
+  const int flat = (sC == 1 && sR == C) ? 1 : 0;
+  dim3 g1(chunks, static_cast<unsigned>(L));
+  const double in_bytes = static_cast<double>(L) * R * C * sizeof(T);
+  cudaError_t e;
+  {
+    LaunchScope scope(kProfNormalize, s, 2.0 * L * R * C, in_bytes);
+    ps::ps_norm_partial_kernel<T><<<g1, ps::NORM_THREADS, 0, s>>>(
+        static_cast<const T*>(x), R, C, sL, sR, sC, flat, chunks, partial);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 1)");
+  const int64_t per_mat_blocks = (Rp * Cp + ps::NORM_THREADS * 8 - 1) / (ps::NORM_THREADS * 8);
+  int64_t gx = (4LL * sms + L - 1) / L;
+  if (gx > per_mat_blocks) gx = per_mat_blocks;
+  if (gx < 1) gx = 1;
+  dim3 g2(static_cast<unsigned>(gx), static_cast<unsigned>(L));
+  {
+    LaunchScope scope(kProfNormalize, s, static_cast<double>(L) * R * C,
+                      in_bytes + 2.0 * L * Rp * Cp);
+    ps::ps_scale_cast_kernel<T><<<g2, ps::NORM_THREADS, 0, s>>>(
+        static_cast<const T*>(x), R, C, sL, sR, sC, flat, partial, chunks, eps,
+        static_cast<__half*>(xh), Rp, Cp);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 2)");
+  return PS_OK;
+}
+
+int64_t normalize_ws_bytes(int64_t L, int64_t rows, int64_t cols, int sms) {
+  return round_up(L * norm_chunks(L, rows, cols, sms) * static_cast<int64_t>(sizeof(double)), 256);
+}
+
+int normalize_impl(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                   int64_t sR, int64_t sC, float eps, void* xh, int64_t Rp, int64_t Cp, void* ws,
+                   int64_t ws_bytes, cudaStream_t stream) {
+  if (!x || !xh || !ws) return fail(PS_ERR_INVALID, "ps_normalize: null pointer");
+  if (!dims_ok(L, rows, cols) || Rp < rows || Cp < cols)
+    return fail(PS_ERR_INVALID, "ps_normalize: bad sizes");
+  if (elem_bytes(x_dtype) == 0) return fail(PS_ERR_INVALID, "ps_normalize: bad dtype");
+  if (!(eps > 0.f)) return fail(PS_ERR_INVALID, "ps_normalize: eps must be positive");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const int chunks = norm_chunks(L, rows, cols, st->sms);
+  if (ws_bytes < normalize_ws_bytes(L, rows, cols, st->sms))
+    return fail(PS_ERR_WORKSPACE, "ps_normalize: workspace too small");
+  double* partial = static_cast<double*>(ws);
+  switch (x_dtype) {
+    case PS_F16:
+      return launch_normalize<__half>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp, partial,
+                                      chunks, st->sms, stream);
+    case PS_BF16:
+      return launch_normalize<__nv_bfloat16>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp,
+                                             partial, chunks, st->sms, stream);
+    case PS_F32:
+      return launch_normalize<float>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp, partial,
+                                     chunks, st->sms, stream);
+    default:
+      return launch_normalize<double>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp, partial,
+                                      chunks, st->sms, stream);
+  }
+}
+
+template <typename T>
+int launch_copy_out(const void* xh, int64_t Rp, int64_t Cp, int64_t R, int64_t C, int64_t L,
+                    void* y, int sms, cudaStream_t s) {
+  int64_t blocks = (L * R * C + ps::NORM_THREADS - 1) / ps::NORM_THREADS;
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  if (blocks < 1) blocks = 1;
+  LaunchScope scope(kProfOther, s, 0.0, static_cast<double>(L) * R * C * (2.0 + sizeof(T)));
+  ps::ps_copy_out_kernel<T><<<static_cast<unsigned>(blocks), ps::NORM_THREADS, 0, s>>>(
+      static_cast<const __half*>(xh), Rp, Cp, R, C, L, static_cast<T*>(y));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "copy-out launch");
+}
+
+int copy_out(const void* xh, int64_t Rp, int64_t Cp, int64_t R, int64_t C, int64_t L, void* y,
+             int y_dtype, int sms, cudaStream_t s) {
+  switch (y_dtype) {
+    case PS_F16:
+      return launch_copy_out<__half>(xh, Rp, Cp, R, C, L, y, sms, s);
+    case PS_BF16:
+      return launch_copy_out<__nv_bfloat16>(xh, Rp, Cp, R, C, L, y, sms, s);
+    case PS_F32:
+      return launch_copy_out<float>(xh, Rp, Cp, R, C, L, y, sms, s);
+    default:
+      return launch_copy_out<double>(xh, Rp, Cp, R, C, L, y, sms, s);
+  }
+}
+
+// ------------------------------------------------------------------ circuit
+struct CircuitLayout {
+  int64_t Rp, Cp, n, m;
+  bool tall;
+  int64_t xh_bytes, buf_bytes, norm_bytes, total;
+};
+
+CircuitLayout circuit_layout(int64_t L, int64_t rows, int64_t cols, int buffers, int sms) {
+  CircuitLayout c;
+  c.Rp = round_up(rows, 8);
+  c.Cp = round_up(cols, 8);
+  c.tall = rows > cols;
+  c.n = c.tall ? c.Cp : c.Rp;
+  c.m = c.tall ? c.Rp : c.Cp;
+  c.xh_bytes = round_up(L * c.Rp * c.Cp * 2, 256);
+  c.buf_bytes = round_up(L * c.n * c.n * 2, 256);
+  c.norm_bytes = normalize_ws_bytes(L, rows, cols, sms);
+  c.total = 2 * c.xh_bytes + buffers * c.buf_bytes + c.norm_bytes;
+  return c;
+}
+
+int validate_table(int n_outer, const float* residuals, const int32_t* n_steps,
+                   const ps_step* steps, int buffers) {
+  if (n_outer <= 0 || !residuals || !n_steps || !steps || buffers < 1)
+    return fail(PS_ERR_INVALID, "ps_circuit: empty circuit");
+  int off = 0;
+  for (int t = 0; t < n_outer; ++t) {
+    if (n_steps[t] <= 0 || !std::isfinite(residuals[t]))
+      return fail(PS_ERR_INVALID,
+                  "ps_circuit: each outer iteration needs a finite residual and at least one "
+                  "inner iteration");
+    unsigned initialized = 1u;  // B[0] holds the Gram matrix
+    for (int s = 0; s < n_steps[t]; ++s) {
+      const ps_step& p = steps[off + s];
+      if (p.dst < 0 || p.src < 0 || p.add < 0 || p.dst >= buffers || p.src >= buffers ||
+          p.add >= buffers || p.dst >= 32 || p.dst == p.src || !(initialized >> p.src & 1u) ||
+          !(initialized >> p.add & 1u) || !std::isfinite(p.alpha) || !std::isfinite(p.beta) ||
+          !std::isfinite(p.diag))
+        return fail(PS_ERR_INVALID, "ps_circuit: invalid inner iteration %d of outer %d", s, t);
+      initialized |= 1u << p.dst;
+    }
+    off += n_steps[t];
+  }
+  return PS_OK;
+}
+
+// Workspace layout of a grouped circuit: per problem two FP16 copies of X
+// (padded to multiples of 8), the square buffers of all problems that share
+// the same n stacked so one launch serves them all, and per-problem scratch
+// for the normalisation partial sums.
+struct GroupedPlan {
+  struct Prob {
+    CircuitLayout lay;
+    int group;
+    int64_t goff;          // first matrix of this problem inside its n-group
+    int64_t xh_off[2];
+    int64_t norm_off;
+  };
+  struct NGroup {
+    int64_t n, Ltot, buf_off, buf_bytes;
+  };
+  std::vector<Prob> probs;
+  std::vector<NGroup> groups;
+  int64_t total = 0;
+};
+
+int make_grouped_plan(const ps_problem* probs, int n_probs, int buffers, int sms,
+                      GroupedPlan* plan) {
+  if (!probs || n_probs <= 0 || n_probs > 4096)
+    return fail(PS_ERR_INVALID, "ps_circuit: bad problem list");
+  if (buffers < 1 || buffers > 32) return fail(PS_ERR_INVALID, "ps_circuit: bad buffer count");
+  plan->probs.resize(n_probs);
+  int64_t off = 0;
+  for (int i = 0; i < n_probs; ++i) {
+    const ps_problem& q = probs[i];
+    if (!dims_ok(q.L, q.rows, q.cols)) return fail(PS_ERR_INVALID, "ps_circuit: bad sizes (problem %d)", i);
+    GroupedPlan::Prob& p = plan->probs[i];
+    p.lay = circuit_layout(q.L, q.rows, q.cols, buffers, sms);
+    int g = -1;
+    for (size_t k = 0; k < plan->groups.size(); ++k)
+      if (plan->groups[k].n == p.lay.n) g = static_cast<int>(k);
+    if (g < 0) {
+      plan->groups.push_back({p.lay.n, 0, 0, 0});
+      g = static_cast<int>(plan->groups.size()) - 1;
+    }
+    p.group = g;
+    p.goff = plan->groups[g].Ltot;
+    plan->groups[g].Ltot += q.L;
+    p.xh_off[0] = off;
+    p.xh_off[1] = off + p.lay.xh_bytes;
+    off += 2 * p.lay.xh_bytes;
+  }
+  for (GroupedPlan::NGroup& g : plan->groups) {
+    g.buf_bytes = round_up(g.Ltot * g.n * g.n * 2, 256);
+    g.buf_off = off;
+    off += buffers * g.buf_bytes;
+  }
+  for (GroupedPlan::Prob& p : plan->probs) {
+    p.norm_off = off;
+    off += p.lay.norm_bytes;
+  }
+  plan->total = off;
+  return PS_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int ps_version(void) { return kVersion; }
+
+const char* ps_last_error(void) { return g_last_error.c_str(); }
+
+int ps_get_status(int* status, int clear) {
+  if (!status) return fail(PS_ERR_INVALID, "ps_get_status: null pointer");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaError_t e = cudaMemcpy(status, st->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (clear) {
+    e = cudaMemset(st->status, 0, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "clear status");
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "clear status");
+  }
+  return PS_OK;
+}
+
+long long ps_launch_count(void) { return g_launches.load(); }
+
+int ps_profile_enable(int enable) {
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  if (enable) {
+    for (ProfRecord& r : g_prof) {
+      g_event_pool.push_back(r.start);
+      g_event_pool.push_back(r.stop);
+    }
+    g_prof.clear();
+  }
+  g_prof_on = enable != 0;
+  return PS_OK;
+}
+
+int ps_profile_read(int kind, double* total_ms, int64_t* launches, double* flops, double* bytes) {
+  if (kind < 0 || kind >= kNumProfKinds || !total_ms || !launches || !flops || !bytes)
+    return fail(PS_ERR_INVALID, "ps_profile_read: bad arguments");
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  double ms = 0.0, f = 0.0, b = 0.0;
+  int64_t n = 0;
+  for (const ProfRecord& r : g_prof) {
+    if (r.kind != kind) continue;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "ps_profile_read");
+    float t = 0.f;
+    e = cudaEventElapsedTime(&t, r.start, r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "ps_profile_read");
+    ms += t;
+    f += r.flops;
+    b += r.bytes;
+    ++n;
+  }
+  *total_ms = ms;
+  *launches = n;
+  *flops = f;
+  *bytes = b;
+  return PS_OK;
+}
+
+int ps_set_wait_limit(long long cycles) {
+  if (cycles <= 0) return fail(PS_ERR_INVALID, "ps_set_wait_limit: cycles must be positive");
+  g_wait_limit = cycles;
+  return PS_OK;
+}
+
+int ps_selftest_wait(long long limit_cycles, void* stream) {
+  if (limit_cycles <= 0) return fail(PS_ERR_INVALID, "ps_selftest_wait: limit must be positive");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  ps::ps_selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(st->status,
+                                                                               limit_cycles);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "selftest launch");
+}
+
+int64_t ps_normalize_workspace_bytes(int64_t L, int64_t rows, int64_t cols) {
+  DeviceState* st = nullptr;
+  if (device_state(&st)) return -1;
+  if (!dims_ok(L, rows, cols)) return -1;
+  return normalize_ws_bytes(L, rows, cols, st->sms);
+}
+
+int ps_normalize(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                 int64_t sR, int64_t sC, float eps, void* xh, int64_t rows_p, int64_t cols_p,
+                 void* workspace, int64_t workspace_bytes, void* stream) {
+  return normalize_impl(x, x_dtype, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
+                        workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ps_gram(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
+            void* stream) {
+  return gram_impl(x, out, L, rows, cols, x_ld, rows > cols, static_cast<cudaStream_t>(stream));
+}
+
+int ps_square(const void* a, const void* c, void* out, int64_t L, int64_t n, float alpha,
+              float beta, float diag, void* stream) {
+  return sym_product_impl(a, a, c, out, L, n, alpha, beta, diag,
+                          static_cast<cudaStream_t>(stream), "ps_square");
+}
+
+int ps_sym_product(const void* p, const void* q, const void* c, void* out, int64_t L, int64_t n,
+                   float alpha, float beta, float diag, void* stream) {
+  return sym_product_impl(p, q, c, out, L, n, alpha, beta, diag,
+                          static_cast<cudaStream_t>(stream), "ps_sym_product");
+}
+
+int ps_apply(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
+             int64_t x_ld, float residual, int y_dtype, int64_t y_ld, void* stream) {
+  return apply_impl(b, x, y, L, rows, cols, x_ld, residual, y_dtype, y_ld, rows > cols,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int ps_add_diag(const void* in, void* out, int64_t L, int64_t n, float a, void* stream) {
+  if (!in || !out) return fail(PS_ERR_INVALID, "ps_add_diag: null pointer");
+  if (!dims_ok(L, n, n)) return fail(PS_ERR_INVALID, "ps_add_diag: bad sizes");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int64_t blocks = (L * n * n + ps::NORM_THREADS - 1) / ps::NORM_THREADS;
+  if (blocks > 8LL * st->sms) blocks = 8LL * st->sms;
+  LaunchScope scope(kProfOther, static_cast<cudaStream_t>(stream), 0.0, 4.0 * L * n * n);
+  ps::ps_add_diag_kernel<<<static_cast<unsigned>(blocks), ps::NORM_THREADS, 0,
+                           static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(in), static_cast<__half*>(out), L, n, a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "add_diag launch");
+}
+
+int64_t ps_circuit_workspace_bytes(int64_t L, int64_t rows, int64_t cols, int buffers) {
+  ps_problem p;
+  std::memset(&p, 0, sizeof(p));
+  p.L = L;
+  p.rows = rows;
+  p.cols = cols;
+  return ps_circuit_grouped_workspace_bytes(&p, 1, buffers);
+}
+
+int ps_circuit(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+               int64_t sR, int64_t sC, void* y, int y_dtype, int n_outer,
+               const float* residuals, const int32_t* n_steps, const ps_step* steps, int buffers,
+               float eps, void* workspace, int64_t workspace_bytes, void* stream) {
+  ps_problem p;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.L = L;
+  p.rows = rows;
+  p.cols = cols;
+  p.sL = sL;
+  p.sR = sR;
+  p.sC = sC;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  return ps_circuit_grouped(&p, 1, n_outer, residuals, n_steps, steps, buffers, eps, workspace,
+                            workspace_bytes, stream);
+}
+
+int64_t ps_circuit_grouped_workspace_bytes(const ps_problem* probs, int n_probs, int buffers) {
+  DeviceState* st = nullptr;
+  if (device_state(&st)) return -1;
+  GroupedPlan plan;
+  if (make_grouped_plan(probs, n_probs, buffers, st->sms, &plan)) return -1;
+  return plan.total;
+}
+
+int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const float* residuals,
+                       const int32_t* n_steps, const ps_step* steps, int buffers, float eps,
+                       void* workspace, int64_t workspace_bytes, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!workspace) return fail(PS_ERR_INVALID, "ps_circuit: null workspace");
+  int rc = validate_table(n_outer, residuals, n_steps, steps, buffers);
+  if (rc) return rc;
+  for (int i = 0; i < n_probs; ++i)
+    if (!probs[i].x || !probs[i].y) return fail(PS_ERR_INVALID, "ps_circuit: problem %d has a null pointer", i);
+  DeviceState* st = nullptr;
+  if ((rc = device_state(&st))) return rc;
+  GroupedPlan plan;
+  if ((rc = make_grouped_plan(probs, n_probs, buffers, st->sms, &plan))) return rc;
+  if (workspace_bytes < plan.total) return fail(PS_ERR_WORKSPACE, "ps_circuit: workspace too small");
+  if (!aligned16(workspace)) return fail(PS_ERR_INVALID, "ps_circuit: workspace misaligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int np = n_probs;
+
+  auto buf_ptr = [&](int prob, int b) -> void* {
+    const GroupedPlan::Prob& p = plan.probs[prob];
+    const GroupedPlan::NGroup& g = plan.groups[p.group];
+    return ws + g.buf_off + b * g.buf_bytes + p.goff * p.lay.n * p.lay.n * 2;
+  };
+  std::vector<int> cur(np, 0);
+  std::vector<bool> direct(np);
+  for (int i = 0; i < np; ++i) {
+    const ps_problem& q = probs[i];
+    const GroupedPlan::Prob& p = plan.probs[i];
+    if ((rc = normalize_impl(q.x, q.x_dtype, q.L, q.rows, q.cols, q.sL, q.sR, q.sC, eps,
+                             ws + p.xh_off[0], p.lay.Rp, p.lay.Cp, ws + p.norm_off,
+                             p.lay.norm_bytes, s)))
+      return rc;
+    // The last apply writes straight into y when y's layout allows TMA stores.
+    direct[i] = (q.y_dtype == PS_F16 || q.y_dtype == PS_F32 || q.y_dtype == PS_BF16) &&
+                p.lay.Rp == q.rows && p.lay.Cp == q.cols &&
+                (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 && aligned16(q.y);
+  }
+  int off = 0;
+  for (int t = 0; t < n_outer; ++t) {
+    for (int i = 0; i < np; ++i) {
+      const GroupedPlan::Prob& p = plan.probs[i];
+      if ((rc = gram_impl(ws + p.xh_off[cur[i]], buf_ptr(i, 0), probs[i].L, p.lay.Rp, p.lay.Cp,
+                          p.lay.Cp, p.lay.tall, s)))
+        return rc;
+    }
+    int last = 0;
+    for (int k = 0; k < n_steps[t]; ++k) {
+      const ps_step& q = steps[off + k];
+      // One launch per distinct n covers the inner iteration of every problem.
+      for (const GroupedPlan::NGroup& g : plan.groups) {
+        uint8_t* base = ws + g.buf_off;
+        if ((rc = sym_product_impl(base + q.src * g.buf_bytes, base + q.src * g.buf_bytes,
+                                   base + q.add * g.buf_bytes, base + q.dst * g.buf_bytes, g.Ltot,
+                                   g.n, q.alpha, q.beta, q.diag, s, "ps_circuit(square)")))
+          return rc;
+      }
+      last = q.dst;
+    }
+    off += n_steps[t];
+    const bool final_iter = t == n_outer - 1;
+    for (int i = 0; i < np; ++i) {
+      const GroupedPlan::Prob& p = plan.probs[i];
+      const ps_problem& q = probs[i];
+      const int64_t Rp = p.lay.Rp, Cp = p.lay.Cp;
+      if (final_iter && direct[i]) {
+        rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], q.y, q.L, Rp, Cp, Cp,
+                        residuals[t], q.y_dtype, q.cols, p.lay.tall, s);
+      } else {
+        rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], ws + p.xh_off[1 - cur[i]], q.L,
+                        Rp, Cp, Cp, residuals[t], PS_F16, Cp, p.lay.tall, s);
+        cur[i] = 1 - cur[i];
+      }
+      if (rc) return rc;
+    }
+  }
+  for (int i = 0; i < np; ++i) {
+    if (direct[i]) continue;
+    const GroupedPlan::Prob& p = plan.probs[i];
+    const ps_problem& q = probs[i];
+    if ((rc = copy_out(ws + p.xh_off[cur[i]], p.lay.Rp, p.lay.Cp, q.rows, q.cols, q.L, q.y,
+                       q.y_dtype, st->sms, s)))
+      return rc;
+  }
+  return PS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,470 @@
+// One persistent, warp-specialised tcgen05 GEMM family that implements every
+// dense contraction of a Polar Switch circuit:
+//
+//   symmetric  D = alpha * A . B^T + beta * C + diag * I     (gram, square,
+//              only tiles on or above the block diagonal are computed; the
+//              epilogue writes each off-diagonal 128x128 block twice, once
+//              transposed)
+//   general    D = A . B^T + beta * C                          (apply)
+//
+// Operands are FP16 in HBM, staged by TMA into 128-byte-swizzled shared
+// memory, multiplied by tcgen05.mma (kind::f16) into FP32 accumulators in
+// TMEM, and the epilogue does alpha/beta*C/diag in FP32 followed by exactly
+// one rounding to FP16 (optionally widened to FP32/BF16 for the final output).
+//
+// Roles (192 threads, one CTA per SM, persistent over a static tile list):
+//   warp 0 lane 0   TMA producer, STAGES-deep smem ring
+//   warp 1          TMEM allocator; lane 0 issues the UMMAs
+//   warps 2..5      epilogue: tcgen05.ld -> FP32 math -> swizzled smem ->
+//                   TMA store (plus the mirrored store for symmetric tiles)
+//
+// Reference behaviour this follows: polar_switch/triton_kernels.py:24-57 (one
+// owner per symmetric tile, FP32 epilogue alpha*acc + beta*C then + diag,
+// single FP16 store and a transposed mirror store) and
+// polar_switch/gemm_symmetric_fused.py:45-76 (mirror only off the diagonal,
+// diagonal shift only where the tile meets the diagonal).
+#pragma once
+
+#include "ps_ptx.cuh"
+
+namespace ps {
+
+constexpr int BM = 128;           // UMMA M (TMEM lanes)
+constexpr int BN = 256;           // UMMA N (TMEM columns per accumulator)
+constexpr int BK = 64;            // 64 halves = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int UMMA_K = 16;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int MN_ATOM_BYTES = 64 * BK * 2;  // one 64(MN) x 64(K) MN-major box: 8 KB
+constexpr int NUM_EPI_WARPS = 4;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr int EPI_WARP_BYTES = 8192;
+constexpr int SMEM_OPERANDS = STAGES * STAGE_BYTES;
+constexpr int SMEM_EPI = NUM_EPI_WARPS * EPI_WARP_BYTES;
+constexpr int SMEM_CTRL = 256;
+constexpr int SMEM_TOTAL = SMEM_OPERANDS + SMEM_EPI + SMEM_CTRL + 1024;  // +1 KB alignment slack
+constexpr uint32_t TMEM_COLS = 2 * BN;   // double-buffered accumulator
+constexpr long long kDefaultWaitLimit = 1ll << 32;  // ~2 s of SM clock
+
+enum OutType : int { kOutF16 = 0, kOutF32 = 1, kOutBF16 = 2 };
+
+struct GemmArgs {
+  int M, N, K, L;            // D is M x N per matrix, L matrices
+  int tiles_m, tiles_n;      // general mode: tile grid
+  int tb;                    // symmetric mode: number of 128-row blocks
+  int tiles_per_mat, total_tiles;
+  int group_m;               // general mode: M-tiles per rasterisation group
+  float alpha, beta, diag;
+  const __half* C;           // addend (FP16), may alias D in symmetric mode
+  long long c_ld, c_bs;      // addend leading dimension / batch stride (elements)
+  int has_addend, has_diag;
+  int* status;               // device status word
+  long long wait_limit;      // cycles before a bounded wait gives up
+};
+
+template <bool SYM>
+__device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& b, int& m0, int& n0) {
+  b = t / a.tiles_per_mat;
+  int r = t - b * a.tiles_per_mat;
+  if (SYM) {
+    // Row bi owns ceil((tb - bi) / 2) tiles starting at block column bi.
+    int bi = 0;
+    while (true) {
+      const int cnt = (a.tb - bi + 1) >> 1;
+      if (r < cnt) break;
+      r -= cnt;
+      ++bi;
+    }
+    m0 = bi * BM;
+    n0 = (bi + 2 * r) * BM;
+  } else {
+    const int per_group = a.group_m * a.tiles_n;
+    const int g = r / per_group;
+    const int first = g * a.group_m;
+    const int gsz = min(a.group_m, a.tiles_m - first);
+    const int idx = r - g * per_group;
+    m0 = (first + idx % gsz) * BM;
+    n0 = (idx / gsz) * BN;
+  }
+}
+
+template <int OUT>
+struct OutTraits;
+template <>
+struct OutTraits<kOutF16> {
+  static constexpr int kBytes = 2;
+};
+template <>
+struct OutTraits<kOutBF16> {
+  static constexpr int kBytes = 2;
+};
+template <>
+struct OutTraits<kOutF32> {
+  static constexpr int kBytes = 4;
+};
+
+// Convert 32 FP32 values of one output row to the output type, rounding to
+// FP16 first (the circuit's single rounding) and widening afterwards.
+template <int OUT>
+__device__ __forceinline__ void convert_row(const float (&f)[32], uint32_t (&w)[32]) {
+  if (OUT == kOutF16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = pack_half2(f[2 * j], f[2 * j + 1]);
+  } else if (OUT == kOutBF16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float lo = __half2float(__float2half_rn(f[2 * j]));
+      const float hi = __half2float(__float2half_rn(f[2 * j + 1]));
+      __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(__half2float(__float2half_rn(f[j])));
+  }
+}
+
+template <bool A_MN, bool B_MN, bool SYM, int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    ps_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* s_epi = smem + SMEM_OPERANDS;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_epi + SMEM_EPI);
+  uint64_t* full = bars;                  // [STAGES]
+  uint64_t* empty = bars + STAGES;        // [STAGES]
+  uint64_t* tfull = bars + 2 * STAGES;    // [2]
+  uint64_t* tempty = tfull + 2;           // [2]
+  uint64_t* drain = tempty + 2;           // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], NUM_EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_kb = (args.K + BK - 1) / BK;
+  const int ncols_total = args.N;  // symmetric: N == M
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+        int b, m0, n0;
+        decode_tile<SYM>(args, t, b, m0, n0);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status,
+                                 kStatusProducerTimeout, args.wait_limit)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + stage * STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_3d(&tmA, a_dst, &full[stage], k0, m0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_3d(&tmA, a_dst + j * MN_ATOM_BYTES, &full[stage], m0 + 64 * j, k0, b);
+          }
+          if (!B_MN) {
+            tma_load_3d(&tmB, b_dst, &full[stage], k0, n0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(&tmB, b_dst + j * MN_ATOM_BYTES, &full[stage], n0 + 64 * j, k0, b);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load already in flight land before the CTA can exit.
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(issued_mask & (1u << s))) continue;
+          const uint32_t par = (issued_parity >> s) & 1u;
+          const long long start = clock64();
+          while (!mbar_try_wait(&full[s], par)) {
+            if (clock64() - start > args.wait_limit) {
+              if (args.status) atomicCAS(args.status, 0, kStatusDrainTimeout);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+        int b, m0, n0;
+        decode_tile<SYM>(args, t, b, m0, n0);
+        int nvalid = ncols_total - n0;
+        nvalid = nvalid > BN ? BN : nvalid;
+        const int n_mma = (nvalid + 15) & ~15;
+        const uint32_t idesc = make_idesc_f16(BM, n_mma, A_MN, B_MN);
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status,
+                               kStatusMmaTimeout, args.wait_limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.status, kStatusMmaTimeout,
+                                 args.wait_limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t ad = A_MN ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
+                                                            MN_ATOM_BYTES, 1024)
+                                     : make_smem_desc_sw128(a_addr + kk * (UMMA_K * 2), 16, 1024);
+            const uint64_t bd = B_MN ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
+                                                            MN_ATOM_BYTES, 1024)
+                                     : make_smem_desc_sw128(b_addr + kk * (UMMA_K * 2), 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        // Wait for the UMMAs already issued before TMEM is released.
+        umma_commit(drain);
+        const long long start = clock64();
+        while (!mbar_try_wait(drain, 0)) {
+          if (clock64() - start > args.wait_limit) {
+            if (args.status) atomicCAS(args.status, 0, kStatusDrainTimeout);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    constexpr int OB = OutTraits<OUT>::kBytes;
+    constexpr int ROW_BYTES = 32 * OB;              // one staged row: 64 B or 128 B
+    constexpr int BUF_BYTES = 32 * ROW_BYTES;       // 32 x 32 sub-tile
+    constexpr int NBUF = EPI_WARP_BYTES / BUF_BYTES;
+    static_assert(!SYM || OUT == kOutF16, "symmetric products are stored in FP16");
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t stg = smem_u32(s_epi + (warp - 2) * EPI_WARP_BYTES);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+      int b, m0, n0;
+      decode_tile<SYM>(args, t, b, m0, n0);
+      int nvalid = ncols_total - n0;
+      nvalid = nvalid > BN ? BN : nvalid;
+      const int nchunks = (nvalid + 31) >> 5;
+      const int row0 = m0 + 32 * q;       // first row of this warp's 32-row slab
+      const int grow = row0 + lane;       // this thread's output row
+      const bool row_ok = grow < args.M;
+      const bool load_c = args.has_addend && row_ok;
+      const __half* crow =
+          args.has_addend ? args.C + static_cast<long long>(b) * args.c_bs +
+                                static_cast<long long>(grow) * args.c_ld
+                          : nullptr;
+      const int col_end = min(n0 + nvalid, ncols_total);
+      // Pull this thread's addend row into L2 while the UMMAs of the tile run.
+      if (load_c) {
+        for (int cc = n0; cc < col_end; cc += 64) prefetch_l2(crow + cc);
+        prefetch_l2(crow + col_end - 1);
+      }
+      auto load_addend = [&](int c, uint4 (&dst)[4]) {
+        const int g0 = n0 + 32 * c;
+        if (!load_c) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+        } else if (g0 + 32 <= ncols_total) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = ld_global_v4(crow + g0 + 8 * j);
+        } else {
+          __half* hv = reinterpret_cast<__half*>(dst);
+          for (int j = 0; j < 32; ++j)
+            hv[j] = (g0 + j < ncols_total) ? crow[g0 + j] : __float2half(0.f);
+        }
+      };
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, args.status,
+                             kStatusEpilogueTimeout, args.wait_limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint4 cv_next[4];
+      load_addend(0, cv_next);
+      for (int c = 0; c < nchunks; ++c) {
+        const int gcol0 = n0 + 32 * c;
+        // Addend of this chunk was loaded one chunk ahead; start the next one.
+        uint4 cv[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+        if (c + 1 < nchunks) load_addend(c + 1, cv_next);
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                               static_cast<uint32_t>(acc * BN + 32 * c),
+                           v);
+        if (c == nchunks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        float f[32];
+        if (args.has_addend) {
+          const __half* hv = reinterpret_cast<const __half*>(cv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            f[j] = fmaf(args.beta, __half2float(hv[j]), args.alpha * __uint_as_float(v[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = args.alpha * __uint_as_float(v[j]);
+        }
+        if (SYM && args.has_diag) {
+          const int d = grow - gcol0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j == d) f[j] += args.diag;
+        }
+        uint32_t w[32];
+        convert_row<OUT>(f, w);
+
+        // -------- normal store of this 32x32 sub-tile
+        if (lane == 0) bulk_wait_read<NBUF - 1>();
+        __syncwarp();
+        {
+          const uint32_t sb = stg + buf * BUF_BYTES;
+          if (ROW_BYTES == 64) {
+            // 64-byte rows, TMA SWIZZLE_64B: 16 B chunk j -> j ^ ((row >> 1) & 3)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int p = j ^ ((lane >> 1) & 3);
+              st_shared_v4(sb + lane * 64 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                           w[4 * j + 3]);
+            }
+          } else {
+            // 128-byte rows, TMA SWIZZLE_128B: chunk j -> j ^ (row & 7)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int p = j ^ (lane & 7);
+              st_shared_v4(sb + lane * 128 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                           w[4 * j + 3]);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < args.M && gcol0 < ncols_total) tma_store_3d(&tmD, sb, gcol0, row0, b);
+            bulk_commit();
+          }
+          buf = (buf + 1 == NBUF) ? 0 : buf + 1;
+        }
+
+        // -------- mirrored store (symmetric, off the block diagonal)
+        if (SYM && (gcol0 / BM) != (m0 / BM)) {
+          if (lane == 0) bulk_wait_read<NBUF - 1>();
+          __syncwarp();
+          const uint32_t sb = stg + buf * BUF_BYTES;
+          // Transposed sub-tile: row t = column of D, column = lane (row of D).
+          // Lane pairs swap halves so each lane stores 4 bytes.
+          const int odd = lane & 1;
+          const int trow_base = odd;
+          const int tcol = lane & ~1;
+          const int cbyte = tcol * 2;
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const uint32_t mine = w[p];
+            const uint32_t send = odd ? (mine & 0xFFFFu) : (mine >> 16);
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const uint32_t val = odd ? ((recv & 0xFFFFu) | (mine & 0xFFFF0000u))
+                                     : ((mine & 0xFFFFu) | (recv << 16));
+            const int trow = 2 * p + trow_base;
+            const int chunk = (cbyte >> 4) ^ ((trow >> 1) & 3);
+            st_shared_u32(sb + trow * 64 + chunk * 16 + (cbyte & 15), val);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (gcol0 < ncols_total && row0 < args.M) tma_store_3d(&tmD, sb, row0, gcol0, b);
+            bulk_commit();
+          }
+          buf = (buf + 1 == NBUF) ? 0 : buf + 1;
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+}  // namespace ps

@@ -1,0 +1,167 @@
+"""ctypes binding of libpolarswitch_b200.so (the C ABI in include/polar_switch_b200.h).
+
+Torch tensors are used only for device memory and the current CUDA stream; the
+library receives raw pointers, sizes and scalars. There is no fallback: if the
+library is missing or the device is not a B200, calls raise.
+"""
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libpolarswitch_b200.so")
+
+PS_OK = 0
+PS_ERR_INVALID = -1
+PS_ERR_CUDA = -2
+PS_ERR_UNSUPPORTED = -3
+PS_ERR_WORKSPACE = -4
+
+PS_F16, PS_F32, PS_BF16, PS_F64 = 0, 1, 2, 3
+DTYPE_CODES = {torch.float16: PS_F16, torch.float32: PS_F32, torch.bfloat16: PS_BF16, torch.float64: PS_F64}
+
+# Every symbol include/polar_switch_b200.h declares.
+EXPORTED = (
+    "ps_version", "ps_last_error", "ps_get_status", "ps_set_wait_limit", "ps_selftest_wait",
+    "ps_normalize_workspace_bytes", "ps_normalize", "ps_gram", "ps_square", "ps_sym_product",
+    "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
+    "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
+    "ps_profile_enable", "ps_profile_read",
+)
+
+
+class PsStep(ctypes.Structure):
+    """Mirror of `ps_step`: B[dst] = alpha*B[src]@B[src] + beta*B[add] + diag*I."""
+
+    _fields_ = [("dst", ctypes.c_int32), ("src", ctypes.c_int32), ("add", ctypes.c_int32),
+                ("alpha", ctypes.c_float), ("beta", ctypes.c_float), ("diag", ctypes.c_float)]
+
+
+class PsProblem(ctypes.Structure):
+    """Mirror of `ps_problem`: one (L, rows, cols) problem of a grouped circuit."""
+
+    _fields_ = [("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int32), ("L", ctypes.c_int64),
+                ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("sL", ctypes.c_int64),
+                ("sR", ctypes.c_int64), ("sC", ctypes.c_int64), ("y", ctypes.c_void_p),
+                ("y_dtype", ctypes.c_int32)]
+
+
+class NativeError(RuntimeError):
+    """A C-ABI call returned an error status."""
+
+    def __init__(self, name, code, message):
+        super().__init__(f"{name} failed ({code}): {message}")
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+_i64, _f32, _ptr, _int = ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_int
+
+_SIGNATURES = {
+    "ps_version": ([], _int),
+    "ps_last_error": ([], ctypes.c_char_p),
+    "ps_get_status": ([ctypes.POINTER(_int), _int], _int),
+    "ps_set_wait_limit": ([ctypes.c_longlong], _int),
+    "ps_selftest_wait": ([ctypes.c_longlong, _ptr], _int),
+    "ps_normalize_workspace_bytes": ([_i64, _i64, _i64], _i64),
+    "ps_normalize": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _i64, _i64,
+                      _ptr, _i64, _ptr], _int),
+    "ps_gram": ([_ptr, _ptr, _i64, _i64, _i64, _i64, _ptr], _int),
+    "ps_square": ([_ptr, _ptr, _ptr, _i64, _i64, _f32, _f32, _f32, _ptr], _int),
+    "ps_sym_product": ([_ptr, _ptr, _ptr, _ptr, _i64, _i64, _f32, _f32, _f32, _ptr], _int),
+    "ps_apply": ([_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _f32, _int, _i64, _ptr], _int),
+    "ps_add_diag": ([_ptr, _ptr, _i64, _i64, _f32, _ptr], _int),
+    "ps_circuit_workspace_bytes": ([_i64, _i64, _i64, _int], _i64),
+    "ps_circuit": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _int, _int,
+                    ctypes.POINTER(_f32), ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep),
+                    _int, _f32, _ptr, _i64, _ptr], _int),
+    "ps_launch_count": ([], ctypes.c_longlong),
+    "ps_profile_enable": ([_int], _int),
+    "ps_profile_read": ([_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64),
+                         ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], _int),
+    "ps_circuit_grouped_workspace_bytes": ([ctypes.POINTER(PsProblem), _int, _int], _i64),
+    "ps_circuit_grouped": ([ctypes.POINTER(PsProblem), _int, _int, ctypes.POINTER(_f32),
+                            ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep), _int, _f32,
+                            _ptr, _i64, _ptr], _int),
+}
+
+
+def library_path():
+    return _LIB_PATH
+
+
+def load():
+    """Load the shared library (once) and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                raise ImportError(
+                    f"polar_switch native library not built: {_LIB_PATH} is missing "
+                    "(run `python polar-switch_b200/build.py`)")
+            lib = ctypes.CDLL(_LIB_PATH)
+            for name, (args, res) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = lib
+    return _lib
+
+
+def check(name, code):
+    if code != PS_OK:
+        msg = load().ps_last_error().decode(errors="replace")
+        raise NativeError(name, code, msg)
+
+
+def stream_ptr(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def get_status(clear=False):
+    """Device status word of the current device (0 = every bounded wait completed)."""
+    s = ctypes.c_int(0)
+    check("ps_get_status", load().ps_get_status(ctypes.byref(s), 1 if clear else 0))
+    return s.value
+
+
+def set_wait_limit(cycles):
+    check("ps_set_wait_limit", load().ps_set_wait_limit(int(cycles)))
+
+
+def selftest_wait(limit_cycles, device=None):
+    check("ps_selftest_wait", load().ps_selftest_wait(int(limit_cycles), stream_ptr(device)))
+
+
+PROFILE_KINDS = {"normalize": 0, "gram": 1, "square": 2, "apply": 3, "other": 4}
+
+
+def launch_count():
+    """Kernels launched by the library in this process so far."""
+    return int(load().ps_launch_count())
+
+
+def profile_enable(enable=True):
+    check("ps_profile_enable", load().ps_profile_enable(1 if enable else 0))
+
+
+def profile_read():
+    """{kind: dict(ms, launches, flops, bytes)} for the launches recorded since profile_enable()."""
+    out = {}
+    lib = load()
+    for name, k in PROFILE_KINDS.items():
+        ms, n, fl, by = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double(), ctypes.c_double()
+        check("ps_profile_read", lib.ps_profile_read(k, ctypes.byref(ms), ctypes.byref(n),
+                                                     ctypes.byref(fl), ctypes.byref(by)))
+        out[name] = dict(ms=ms.value, launches=n.value, flops=fl.value, bytes=by.value)
+    return out

@@ -1,0 +1,121 @@
+"""GPU tests of Gram Newton-Schulz, the grouped (multi-shape) circuit used by
+the Muon step, the sharded orthogonalizer at world size 1, and the device
+status word of the bounded waits."""
+
+import pytest
+import torch
+
+from oracle import circuit as oc
+from oracle import gns as og
+from polar_switch import coefficients
+from tests._util import seeded
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("shape", [(2, 128, 384), (256, 96), (3, 64, 200)])
+def test_gns_rectangular(cuda_device, shape):
+    from polar_switch import make_polynomial_orthogonalizer
+    from polar_switch.gram_newton_schulz import GNS_COEFFICIENTS
+    X = seeded(shape, 30)
+    polar = make_polynomial_orthogonalizer("GNS")
+    got = polar(X.to(cuda_device)).cpu()
+    assert polar.last_execution["dispatch"] == "rectangular_gram"
+    assert polar.last_execution["effective"] == "GNS"
+    ref64 = og.gns_run(X, GNS_COEFFICIENTS, acc=torch.float64)
+    ref32 = og.gns_run(X, GNS_COEFFICIENTS, acc=torch.float32)
+    err = oc.relative_frobenius(got, ref64)
+    floor = oc.relative_frobenius(ref32, ref64)
+    assert err <= max(5e-3, 1.5 * floor), (err, floor)
+    lo, hi = oc.singular_interval(got)
+    rlo, rhi = oc.singular_interval(ref64)
+    assert abs(lo - rlo) <= 1e-3 and abs(hi - rhi) <= 1e-3
+    # published GNS interval [0.787021, 1.212979] for sigma in [1e-3, 1]
+    assert 0.787 - 2e-3 <= lo and hi <= 1.213 + 2e-3
+
+
+def test_gns_square_uses_polar_express(cuda_device):
+    from polar_switch import make_polynomial_orthogonalizer
+    X = seeded((192, 192), 31)
+    polar = make_polynomial_orthogonalizer("GNS")
+    got = polar(X.to(cuda_device)).cpu()
+    assert polar.last_execution["dispatch"] == "square_polar_express"
+    assert polar.last_execution["effective"] == "POLAR_EXPRESS"
+    ref = oc.run_circuit(X, coefficients.POLAR_EXPRESS, acc=torch.float64)
+    assert oc.relative_frobenius(got, ref) <= 5e-3
+
+
+def test_grouped_matches_single_calls(cuda_device):
+    """Muon buckets of different shapes in one grouped call = separate calls, bit for bit."""
+    from polar_switch import make_polynomial_orthogonalizer
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    banks = [seeded((3, 256, 128), 40), seeded((2, 128, 128), 41), seeded((2, 128, 384), 42),
+             seeded((1, 200, 96), 43), seeded((4, 64, 256), 44).to(torch.bfloat16)]
+    banks = [b.to(cuda_device) for b in banks]
+    grouped = polar.grouped(banks)
+    for b, g in zip(banks, grouped):
+        single = polar(b)
+        assert g.dtype == b.dtype and g.shape == b.shape
+        assert torch.equal(g, single)
+
+
+def test_grouped_fp16_outputs(cuda_device):
+    from polar_switch import make_polynomial_orthogonalizer
+    polar = make_polynomial_orthogonalizer("PS3_55")
+    banks = [seeded((2, 256, 128), 45).to(cuda_device), seeded((3, 128, 256), 46).to(cuda_device)]
+    outs = [torch.empty(b.shape, device=cuda_device, dtype=torch.float16) for b in banks]
+    polar.grouped(banks, outs=outs)
+    for b, o in zip(banks, outs):
+        assert torch.equal(o.float(), polar(b))
+
+
+def test_sharded_world1_matches_polar(cuda_device):
+    from polar_switch import make_polynomial_orthogonalizer
+    from polar_switch.distributed import ShardedOrthogonalizer
+    shapes = [(3, 256, 128), (4, 128, 128), (2, 128, 384)]
+    banks = [seeded(s, 50 + i).to(cuda_device) for i, s in enumerate(shapes)]
+    sharded = ShardedOrthogonalizer(shapes, method="PS2_55", device=cuda_device, world_size=1, rank=0)
+    sharded(banks)
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    for b, full in zip(banks, sharded.gathered_banks()):
+        assert torch.equal(full.float(), polar(b))
+
+
+def test_status_word_and_bounded_wait(cuda_device):
+    """A kernel whose wait can never complete gives up after its limit and
+    records status 5; the context stays usable afterwards."""
+    from polar_switch import _native as nat
+    with torch.cuda.device(cuda_device):
+        assert nat.get_status(clear=True) in (0, 5)
+        assert nat.get_status() == 0
+        nat.selftest_wait(2_000_000)  # ~1 ms of SM clock
+        torch.cuda.synchronize()
+        assert nat.get_status() == 5
+        assert nat.get_status(clear=True) == 5
+        assert nat.get_status() == 0
+        # the device still computes correctly after the timed-out kernel
+        from polar_switch import make_polynomial_orthogonalizer
+        X = seeded((128, 256), 60)
+        got = make_polynomial_orthogonalizer("PS2_55")(X.to(cuda_device)).cpu()
+        ref = oc.run_circuit(X, coefficients.PS2_55, acc=torch.float64)
+        assert oc.relative_frobenius(got, ref) <= 5e-3
+        assert nat.get_status() == 0
+
+
+def test_launch_counter_and_profiler(cuda_device):
+    from polar_switch import _native as nat
+    from polar_switch import make_polynomial_orthogonalizer
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    X = seeded((2, 256, 512), 61).to(cuda_device)
+    n0 = nat.launch_count()
+    nat.profile_enable(True)
+    polar(X)
+    prof = nat.profile_read()
+    nat.profile_enable(False)
+    # 2 normalise + 2 x (1 gram + 5 squares + 1 apply)
+    assert nat.launch_count() - n0 == 16
+    assert prof["normalize"]["launches"] == 2
+    assert prof["gram"]["launches"] == 2 and prof["square"]["launches"] == 10
+    assert prof["apply"]["launches"] == 2
+    assert prof["square"]["flops"] == pytest.approx(10 * 2 * 256 ** 3)
+    assert all(v["ms"] > 0 for v in prof.values() if v["launches"])

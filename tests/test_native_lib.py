@@ -1,0 +1,48 @@
+"""The C-ABI library loads without a GPU and exports every symbol that
+include/*.h declares (no compute calls here)."""
+
+import ctypes
+import glob
+import os
+import re
+
+from polar_switch import _native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        names.update(re.findall(r"PS_API\s+[\w\s\*]+?\b(ps_\w+)\s*\(", text))
+    return names
+
+
+def test_library_loads_and_exports_all_declared_symbols():
+    lib = _native.load()
+    declared = declared_symbols()
+    assert declared, "no declarations found"
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(_native.EXPORTED) == declared
+
+
+def test_version_and_error_string_without_gpu():
+    lib = _native.load()
+    assert lib.ps_version() >= 100
+    assert isinstance(lib.ps_last_error(), bytes)
+
+
+def test_invalid_arguments_are_rejected_before_any_device_work():
+    lib = _native.load()
+    null = ctypes.c_void_p(0)
+    assert lib.ps_gram(null, null, 1, 8, 8, 8, null) == _native.PS_ERR_INVALID
+    assert b"null" in lib.ps_last_error()
+    assert lib.ps_set_wait_limit(0) == _native.PS_ERR_INVALID
+
+
+def test_struct_layouts_match_header():
+    # ps_step: 3 x int32 + 3 x float; ps_problem: pointers and int64 fields
+    assert ctypes.sizeof(_native.PsStep) == 24
+    assert ctypes.sizeof(_native.PsProblem) == 8 + 8 + 6 * 8 + 8 + 8

@@ -1,0 +1,139 @@
+"""Pin the CPU oracle before trusting it (no GPU needed).
+
+  * Single operations and whole circuits against golden vectors produced by
+    the reference's own Triton kernels and evaluator (run on CPU under
+    TRITON_INTERPRET=1 by tests/golden/make_golden.py).
+  * The port of the reference CPU path against the reference's own output.
+  * GNS against the reference's PyTorch recurrence.
+  * Scalar maps of every table against the published final intervals
+    (reference README.md:64-73, polar_switch/README.md:31-44).
+"""
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import circuit as oc
+from oracle import gns as og
+from oracle import scalar_map as sm
+from oracle.reference_cpu import torch_pe
+from polar_switch import coefficients
+from tests._util import assert_fp16_close
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def load(name):
+    with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
+        return {k: torch.from_numpy(z[k]) if z[k].ndim else z[k].item() for k in z.files}
+
+
+def test_gram_wide_and_tall():
+    g = load("op_gram_wide")
+    assert_fp16_close(oc.gram(g["x"], False), g["out"], what="gram wide")
+    g = load("op_gram_tall")
+    assert_fp16_close(oc.gram(g["x"], True), g["out"], what="gram tall")
+
+
+@pytest.mark.parametrize("name", ["op_square", "op_square_inplace"])
+def test_square(name):
+    g = load(name)
+    got = oc.square(g["a"], g["c"], g["alpha"], g["beta"], g["diag"])
+    assert_fp16_close(got, g["out"], what=name)
+
+
+@pytest.mark.parametrize("name", ["op_apply_wide_nores", "op_apply_wide_res", "op_apply_tall_nores",
+                                  "op_apply_tall_res"])
+def test_apply(name):
+    g = load(name)
+    tall = g["x"].shape[-2] > g["x"].shape[-1]
+    got = oc.apply(g["x"], g["b"], tall, g["residual"])
+    assert_fp16_close(got, g["out"], what=name)
+
+
+CIRCUITS = [("PS2_55", "1x128x256"), ("PS3_55", "1x128x256"), ("POLAR_EXPRESS", "1x128x256"),
+            ("JORDAN", "1x128x256"), ("PS2_55", "2x192x64"), ("PS3_55", "1x96x96"), ("PS2_512", "1x64x160")]
+
+
+@pytest.mark.parametrize("method,shape", CIRCUITS)
+def test_circuit_against_reference_triton(method, shape):
+    g = load(f"circuit_{method}_{shape}")
+    table = getattr(coefficients, method)
+    got = oc.run_circuit(g["x"], table, acc=torch.float32, out_dtype=torch.float16)
+    got64 = oc.run_circuit(g["x"], table, acc=torch.float64, out_dtype=torch.float16)
+    ref = g["out"]
+    # Both are one-rounding evaluations of the same circuit that differ only in
+    # FP32 summation order; the circuits amplify the resulting FP16 rounding
+    # flips, so the bar is the distance between two valid evaluations (FP32
+    # vs FP64 accumulation, measured here), with margin.
+    floor = oc.relative_frobenius(got, got64)
+    err = oc.relative_frobenius(got, ref)
+    assert err <= 1.5 * floor + 5e-4, (err, floor)
+    assert oc.relative_frobenius(got64, ref) <= 1.5 * floor + 5e-4
+    # Singular-value endpoints: the FP64 evaluation (the parity reference of the
+    # GPU tests) within 1e-3 of the reference kernels; the FP32 one within 2e-3
+    # (single rounding flips move the smallest output singular value by ~1e-3).
+    rlo, rhi = oc.singular_interval(ref)
+    lo, hi = oc.singular_interval(got64)
+    assert abs(lo - rlo) < 1e-3 and abs(hi - rhi) < 1e-3
+    lo, hi = oc.singular_interval(got)
+    assert abs(lo - rlo) < 2e-3 and abs(hi - rhi) < 2e-3
+
+
+def test_reference_cpu_path_port_is_exact():
+    g = load("cpu_path_ps2_55_128x256")
+    got = torch_pe(g["x"])
+    assert torch.equal(got, g["out"])
+
+
+def test_gns_against_reference_torch_recurrence():
+    from polar_switch.gram_newton_schulz import GNS_COEFFICIENTS
+    g = load("gns_torch_2x96x224")
+    got = og.gns_run(g["x"], GNS_COEFFICIENTS, acc=torch.float32, mirror=False)
+    err = oc.relative_frobenius(got, g["out"].float())
+    assert err < 3e-3, err
+
+
+PUBLISHED = {
+    "JORDAN": (0.562544, 1.437456), "POLAR_EXPRESS": (0.858872, 1.141128),
+    "PS2_55": (0.872263, 1.106236), "PS2_64": (0.897110, 1.081213), "PS2_54": (0.771715, 1.201363),
+    "PS2_512": (0.894082, 1.091006), "PS2_4111": (0.930600, 1.056149),
+    "PS2_11111": (0.867287, 1.118678), "PS3_55": (0.898309, 1.080954), "PS3_64": (0.913241, 1.070202),
+    "PS3_54": (0.800196, 1.178895),
+}
+
+
+@pytest.mark.parametrize("method", sorted(PUBLISHED))
+def test_scalar_map_published_interval(method):
+    table = getattr(coefficients, method)
+    lo, hi = sm.final_interval(lambda x: sm.circuit_map(table, x))
+    plo, phi = PUBLISHED[method]
+    assert abs(lo - plo) < 2e-6 and abs(hi - phi) < 2e-6, (method, lo, hi)
+
+
+def test_gns_scalar_map_published_interval():
+    from polar_switch.gram_newton_schulz import GNS_COEFFICIENTS
+    lo, hi = sm.final_interval(lambda x: sm.quintic_map(GNS_COEFFICIENTS, x))
+    assert abs(lo - 0.787021) < 2e-6 and abs(hi - 1.212979) < 2e-6, (lo, hi)
+
+
+def test_coefficient_tables_match_reference_data():
+    with open(os.path.join(GOLDEN, "coefficients.json")) as f:
+        ref = json.load(f)
+    for name, table in ref["tables"].items():
+        mine = getattr(coefficients, name)
+        assert json.loads(json.dumps(mine)) == table, name
+    from polar_switch import gram_newton_schulz as gns
+    assert [list(c) for c in gns.GNS_COEFFICIENTS] == ref["gns"]
+    assert [list(c) for c in gns.POLAR_EXPRESS_COEFFICIENTS] == ref["gns_polar_express"]
+
+
+def test_oracle_noise_floor_is_small_on_gaussian_inputs():
+    """FP32 vs FP64 accumulation on N(0,1) input: far below the 5e-3 tolerance."""
+    X = torch.randn(512, 1024, generator=torch.Generator().manual_seed(3))
+    a = oc.run_circuit(X, coefficients.PS2_55, acc=torch.float32)
+    b = oc.run_circuit(X, coefficients.PS2_55, acc=torch.float64)
+    assert oc.relative_frobenius(a, b) < 2e-3
