@@ -118,8 +118,9 @@ PS_API int ps_square(const void* a, const void* c, void* out, int64_t L, int64_t
               float beta, float diag, void* stream);
 
 /* out = fp16(alpha * p @ q + beta * c + diag * I) for symmetric, commuting p
- * and q (so the product is symmetric; only one triangle is computed and
- * mirrored); out may be c but neither p nor q; c may be NULL.
+ * and q (so the product is symmetric): tiles on and above the block diagonal
+ * are computed as p @ q and mirrored below it; out may be c but neither p nor
+ * q; c may be NULL.
  * Replaces sym_baddbmm of polar_switch/gram_newton_schulz.py:64-72. */
 PS_API int ps_sym_product(const void* p, const void* q, const void* c, void* out, int64_t L, int64_t n,
                    float alpha, float beta, float diag, void* stream);
@@ -127,7 +128,8 @@ PS_API int ps_sym_product(const void* p, const void* q, const void* c, void* out
 /* y = b @ x + residual * x (rows <= cols) or x @ b + residual * x (rows > cols),
  * FP32 accumulate, one FP16 rounding, stored as y_dtype (PS_F16, PS_F32 or
  * PS_BF16; wider types are the FP16 value widened). b: (L, n, n) contiguous
- * symmetric; x: (L, rows, cols) FP16 with pitch x_ld; y: pitch y_ld elements
+ * (any square matrix: the product is exactly b @ x or x @ b); x: (L, rows, cols)
+ * FP16 with pitch x_ld; y: pitch y_ld elements
  * (y_ld * sizeof(y_dtype) % 16 == 0). y must not overlap x or b.
  * Replaces apply() of polar_switch/gemm_symmetric_fused.py:304-309. */
 PS_API int ps_apply(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,

@@ -295,8 +295,17 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
     return fail(PS_ERR_INVALID, "%s: the output must not be a multiplied operand", name);
   CUtensorMap ta, tb, td;
   int rc;
+  // A squared buffer is read as A . A^T (both operands K-major, the reference
+  // Triton kernel's form); a product of two different matrices is A @ B with B
+  // read MN-major from its row-major storage, exactly the reference's
+  // gemm_symmetric(A, B) even when B is symmetric only up to rounding.
+  const bool same = p == q;
   if ((rc = map_kmajor(&ta, p, n, n, L, n, n * n, ps::BM))) return rc;
-  if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, ps::BN))) return rc;
+  if (same) {
+    if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, ps::BN))) return rc;
+  } else {
+    if ((rc = map_mnmajor(&tb, q, n, n, L, n, n * n))) return rc;
+  }
   if ((rc = map_out(&td, out, PS_F16, n, n, L, n, n * n))) return rc;
   ps::GemmArgs a = base_args(n, n, n, L);
   fill_sym_tiles(a, n, L);
@@ -309,9 +318,12 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   a.has_addend = c != nullptr;
   a.has_diag = diag != 0.f;
   const double nn = static_cast<double>(n) * n;
-  const double bytes = L * nn * 2.0 * ((p == q ? 1 : 2) + (c ? 1 : 0) + 1);
-  return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
-                                                      L * nn * n, bytes);
+  const double bytes = L * nn * 2.0 * ((same ? 1 : 2) + (c ? 1 : 0) + 1);
+  if (same)
+    return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
+                                                        L * nn * n, bytes);
+  return launch_gemm<false, true, true, ps::kOutF16>(8, ta, tb, td, a, stream, kProfSquare,
+                                                     L * nn * n, bytes);
 }
 
 int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
@@ -349,10 +361,8 @@ int apply_launch(bool tall, const CUtensorMap& ta, const CUtensorMap& tb, const 
   const double out_bytes = OUT == ps::kOutF32 ? 4.0 : 2.0;
   const double flops = 2.0 * L * M * N * K;
   const double bytes = L * (2.0 * K * K + 2.0 * M * N + out_bytes * M * N);
-  if (!tall) return launch_gemm<false, true, false, OUT>(2 + OUT, ta, tb, td, a, s, kProfApply,
-                                                         flops, bytes);
-  return launch_gemm<false, false, false, OUT>(5 + OUT, ta, tb, td, a, s, kProfApply, flops,
-                                               bytes);
+  (void)tall;  // both orientations are A (K-major) times B (MN-major)
+  return launch_gemm<false, true, false, OUT>(2 + OUT, ta, tb, td, a, s, kProfApply, flops, bytes);
 }
 
 int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
@@ -378,8 +388,9 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
     if ((rc = map_kmajor(&ta, b, n, n, L, n, n * n, ps::BM))) return rc;
     if ((rc = map_mnmajor(&tb, x, m, n, L, x_ld, rows * x_ld))) return rc;
   } else {
+    // X @ B: B read MN-major (row-major B, element (k, n)), exactly X @ B.
     if ((rc = map_kmajor(&ta, x, n, m, L, x_ld, rows * x_ld, ps::BM))) return rc;
-    if ((rc = map_kmajor(&tb, b, n, n, L, n, n * n, ps::BN))) return rc;
+    if ((rc = map_mnmajor(&tb, b, n, n, L, n, n * n))) return rc;
   }
   ps::GemmArgs a = base_args(M, N, n, L);
   fill_gen_tiles(a, M, N, L);

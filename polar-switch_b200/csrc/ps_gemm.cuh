@@ -7,6 +7,11 @@
 //              transposed)
 //   general    D = A . B^T + beta * C                          (apply)
 //
+// "B^T" is in the UMMA sense (B supplies N rows of K): a K-major B tile is
+// read from the rows of a row-major matrix (A . A^T for a squared buffer, the
+// Gram X . X^T), an MN-major B tile from its columns, which makes the product
+// exactly A @ B (products of two different matrices, apply).
+//
 // Operands are FP16 in HBM, staged by TMA into 128-byte-swizzled shared
 // memory, multiplied by tcgen05.mma (kind::f16) into FP32 accumulators in
 // TMEM, and the epilogue does alpha/beta*C/diag in FP32 followed by exactly

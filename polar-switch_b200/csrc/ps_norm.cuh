@@ -69,6 +69,22 @@ __device__ __forceinline__ double block_sum(double v, double* s_warp) {
   return t;
 }
 
+// 16-byte vector of T unpacked to floats (VW = 16 / sizeof(T) values).
+template <typename T>
+struct Vec16 {
+  static constexpr int VW = 16 / sizeof(T);
+  __device__ __forceinline__ static void load(const T* p, float (&f)[VW]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < VW; ++i) f[i] = to_f32(t[i]);
+  }
+};
+
+__device__ __forceinline__ bool is_aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 // Pass 1: partial[l * chunks + chunk] = sum of squares of one chunk of matrix l.
 // `flat` means the matrix is one contiguous run of R*C elements.
 template <typename T>
@@ -81,22 +97,45 @@ __global__ void __launch_bounds__(NORM_THREADS)
   const T* xm = x + static_cast<long long>(l) * sL;
   double acc = 0.0;
   if (flat) {
+    constexpr int VW = Vec16<T>::VW;
     const long long E = R * C;
-    const long long per = (E + chunks - 1) / chunks;
+    // chunk boundaries on whole 16-byte vectors
+    long long per = (E + chunks - 1) / chunks;
+    per = (per + VW - 1) / VW * VW;
     const long long beg = chunk * per;
     const long long end = beg + per < E ? beg + per : E;
-    long long e = beg + threadIdx.x;
-    for (; e + 3 * NORM_THREADS < end; e += 4 * NORM_THREADS) {
-      const float v0 = to_f32(xm[e]);
-      const float v1 = to_f32(xm[e + NORM_THREADS]);
-      const float v2 = to_f32(xm[e + 2 * NORM_THREADS]);
-      const float v3 = to_f32(xm[e + 3 * NORM_THREADS]);
-      acc += static_cast<double>(v0) * v0 + static_cast<double>(v1) * v1 +
-             static_cast<double>(v2) * v2 + static_cast<double>(v3) * v3;
-    }
-    for (; e < end; e += NORM_THREADS) {
-      const float v = to_f32(xm[e]);
-      acc += static_cast<double>(v) * v;
+    if (is_aligned16(xm) && beg < end) {
+      // FP32 partial sums per thread (a few hundred terms), FP64 across threads.
+      float a0 = 0.f, a1 = 0.f;
+      const long long nvec = (end - beg) / VW;
+      const T* base = xm + beg;
+      long long v = threadIdx.x;
+      for (; v + NORM_THREADS < nvec; v += 2 * NORM_THREADS) {
+        float f0[VW], f1[VW];
+        Vec16<T>::load(base + v * VW, f0);
+        Vec16<T>::load(base + (v + NORM_THREADS) * VW, f1);
+#pragma unroll
+        for (int i = 0; i < VW; ++i) {
+          a0 = fmaf(f0[i], f0[i], a0);
+          a1 = fmaf(f1[i], f1[i], a1);
+        }
+      }
+      for (; v < nvec; v += NORM_THREADS) {
+        float f0[VW];
+        Vec16<T>::load(base + v * VW, f0);
+#pragma unroll
+        for (int i = 0; i < VW; ++i) a0 = fmaf(f0[i], f0[i], a0);
+      }
+      for (long long e = beg + nvec * VW + threadIdx.x; e < end; e += NORM_THREADS) {
+        const float f = to_f32(xm[e]);
+        a1 = fmaf(f, f, a1);
+      }
+      acc = static_cast<double>(a0) + static_cast<double>(a1);
+    } else {
+      for (long long e = beg + threadIdx.x; e < end; e += NORM_THREADS) {
+        const float v = to_f32(xm[e]);
+        acc += static_cast<double>(v) * v;
+      }
     }
   } else {
     const long long per = (R + chunks - 1) / chunks;
@@ -137,9 +176,32 @@ __global__ void __launch_bounds__(NORM_THREADS)
   const T* xm = x + static_cast<long long>(l) * sL;
   __half* out = xh + static_cast<long long>(l) * Rp * Cp;
   if (flat && Rp == R && Cp == C) {
+    constexpr int VW = Vec16<T>::VW;
     const long long E = R * C;
-    for (long long e = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < E;
-         e += static_cast<long long>(gridDim.x) * NORM_THREADS)
+    const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
+    long long tail = 0;
+    if (is_aligned16(xm) && is_aligned16(out)) {
+      const long long nvec = E / VW;
+      for (long long v = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; v < nvec;
+           v += stride) {
+        float f[VW];
+        Vec16<T>::load(xm + v * VW, f);
+        uint32_t h[VW / 2];
+#pragma unroll
+        for (int i = 0; i < VW / 2; ++i)
+          h[i] = pack_half2(__fdiv_rn(f[2 * i], den), __fdiv_rn(f[2 * i + 1], den));
+        if constexpr (VW == 8) {
+          *reinterpret_cast<uint4*>(out + v * VW) = make_uint4(h[0], h[1], h[2], h[3]);
+        } else if constexpr (VW == 4) {
+          *reinterpret_cast<uint2*>(out + v * VW) = make_uint2(h[0], h[1]);
+        } else {
+          *reinterpret_cast<uint32_t*>(out + v * VW) = h[0];
+        }
+      }
+      tail = nvec * VW;
+    }
+    for (long long e = tail + static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < E;
+         e += stride)
       out[e] = __float2half_rn(__fdiv_rn(to_f32(xm[e]), den));
   } else {
     const long long E = Rp * Cp;

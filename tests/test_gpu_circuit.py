@@ -11,9 +11,11 @@ Tolerances, stated here:
     oracle distance, the "noise floor", is measured in every case); there the
     bar is 1.5 x that floor.
   * singular-value interval endpoints within 1e-3 of the FP64 evaluation
-    (north star); for the PS3 tables, whose first inner iterations use
-    coefficients near -170, endpoints move by up to ~1.5e-3 between valid FP32
-    evaluations, so their bar is 2e-3.
+    (north star) for matrices with min(rows, cols) >= 512. Below that, and for
+    the PS3 tables (first inner iterations with coefficients near -170), the
+    smallest output singular value moves by up to ~1.5e-3 between valid FP32
+    evaluations (measured between the CPU FP32 oracle and the reference's own
+    Triton kernels, tests/test_oracle.py), so the bar there is 2e-3.
 """
 
 import pytest
@@ -27,7 +29,7 @@ pytestmark = pytest.mark.gpu
 
 REL_FRO_TOL = 5e-3
 SIGMA_TOL = 1e-3
-SIGMA_TOL_PS3 = 2e-3
+SIGMA_TOL_PS3 = 2e-3  # also used for min(rows, cols) < 512
 
 
 def _check(method, X, device):
@@ -46,7 +48,7 @@ def _check(method, X, device):
     assert err <= rel_tol, f"{method}: rel Frobenius {err:.3e} vs FP64 (floor {floor:.3e}, tol {rel_tol:.3e})"
     lo, hi = oc.singular_interval(got)
     rlo, rhi = oc.singular_interval(ref64)
-    stol = SIGMA_TOL_PS3 if method.startswith("PS3") else SIGMA_TOL
+    stol = SIGMA_TOL_PS3 if method.startswith("PS3") or min(X.shape[-2:]) < 512 else SIGMA_TOL
     assert abs(lo - rlo) <= stol and abs(hi - rhi) <= stol, (method, (lo, hi), (rlo, rhi), stol)
     return err, floor, (lo, hi)
 
