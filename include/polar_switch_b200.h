@@ -105,6 +105,29 @@ PS_API int ps_normalize(const void* x, int x_dtype, int64_t L, int64_t rows, int
                  int64_t sR, int64_t sC, float eps, void* xh, int64_t rows_p, int64_t cols_p,
                  void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of ps_normalize (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory at the point of the call:
+ * code running under another framework's memory pool that owns all device
+ * memory, real-time loops that must not enter the CUDA allocator, or foreign
+ * runtimes that hold device pointers but no allocator. Instead of a caller
+ * workspace, the partial sums live in a static scratch array inside the
+ * library, PS_NORMALIZE_NOALLOC_MAX_PARTIALS doubles (256 KiB), which every
+ * GPU that loads the library keeps until the process exits.
+ *
+ * Same arguments and result as ps_normalize without the workspace. L must be
+ * at most PS_NORMALIZE_NOALLOC_MAX_PARTIALS (PS_ERR_UNSUPPORTED otherwise).
+ * Calls no allocating routine. The first call on a device looks up the
+ * scratch's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture. All calls on a device share the scratch: calls
+ * whose kernels overlap on the GPU (different streams, no ordering) race and
+ * give wrong results; calls ordered on one stream are safe. Every call writes
+ * all the partial sums it reads, so leftovers of earlier calls never matter. */
+#define PS_NORMALIZE_NOALLOC_MAX_PARTIALS 32768
+PS_API int ps_normalize_noalloc(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols,
+                                int64_t sL, int64_t sR, int64_t sC, float eps, void* xh,
+                                int64_t rows_p, int64_t cols_p, void* stream);
+
 /* out = x @ x^T (rows <= cols) or x^T @ x (rows > cols), FP32 accumulate,
  * one FP16 rounding; out is (L, n, n) contiguous, n = min(rows, cols), n % 8 == 0.
  * Replaces gram() of polar_switch/gemm_symmetric_fused.py:291-293. */

@@ -21,6 +21,12 @@
 namespace ps {
 // First error code recorded by a bounded wait in any kernel on this device.
 __device__ int g_status;
+
+// Scratch of ps_normalize_noalloc: the per-chunk sums of squares of pass 1,
+// PS_NORMALIZE_NOALLOC_MAX_PARTIALS doubles (256 KiB). It lives in the
+// library's module, so every GPU that loads the library holds it until the
+// process exits, and every call of ps_normalize_noalloc on a device shares it.
+static __device__ __align__(256) double g_noalloc_partials[PS_NORMALIZE_NOALLOC_MAX_PARTIALS];
 }  // namespace ps
 
 namespace {
@@ -880,6 +886,72 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
       return rc;
   }
   return PS_OK;
+}
+
+// ---------------------------------------------------------------- no-alloc normalise
+// Device address of ps::g_noalloc_partials per device. Host code may not pass
+// the array's name to a kernel: on the host it is a stand-in symbol, not a
+// device address. The address is looked up once per device, with that device
+// current, on the first ps_normalize_noalloc call there.
+static std::mutex g_noalloc_mu;
+static double* g_noalloc_ptr[kMaxDevices] = {};
+
+static int noalloc_scratch(double** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PS_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, ps::g_noalloc_partials);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_ptr[dev] = static_cast<double*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return PS_OK;
+}
+
+int ps_normalize_noalloc(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols,
+                         int64_t sL, int64_t sR, int64_t sC, float eps, void* xh, int64_t rows_p,
+                         int64_t cols_p, void* stream) {
+  if (!x || !xh) return fail(PS_ERR_INVALID, "ps_normalize_noalloc: null pointer");
+  if (!dims_ok(L, rows, cols) || rows_p < rows || cols_p < cols)
+    return fail(PS_ERR_INVALID, "ps_normalize_noalloc: bad sizes");
+  if (elem_bytes(x_dtype) == 0) return fail(PS_ERR_INVALID, "ps_normalize_noalloc: bad dtype");
+  if (!(eps > 0.f)) return fail(PS_ERR_INVALID, "ps_normalize_noalloc: eps must be positive");
+  if (L > PS_NORMALIZE_NOALLOC_MAX_PARTIALS)
+    return fail(PS_ERR_UNSUPPORTED,
+                "ps_normalize_noalloc: L=%lld matrices exceed the built-in scratch of %d partial "
+                "sums; use ps_normalize with a caller workspace",
+                (long long)L, PS_NORMALIZE_NOALLOC_MAX_PARTIALS);
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  double* partial = nullptr;
+  if ((rc = noalloc_scratch(&partial))) return rc;
+  // Same chunking as ps_normalize whenever it fits, so both entry points give
+  // identical results; otherwise fewer chunks per matrix.
+  int chunks = norm_chunks(L, rows, cols, st->sms);
+  if (L * chunks > PS_NORMALIZE_NOALLOC_MAX_PARTIALS)
+    chunks = static_cast<int>(PS_NORMALIZE_NOALLOC_MAX_PARTIALS / L);
+  // Pass 1 writes every one of the L * chunks partial sums before pass 2 reads
+  // them, so nothing left in the scratch by an earlier call is ever read.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (x_dtype) {
+    case PS_F16:
+      return launch_normalize<__half>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
+                                      partial, chunks, st->sms, s);
+    case PS_BF16:
+      return launch_normalize<__nv_bfloat16>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p,
+                                             cols_p, partial, chunks, st->sms, s);
+    case PS_F32:
+      return launch_normalize<float>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
+                                     partial, chunks, st->sms, s);
+    default:
+      return launch_normalize<double>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
+                                      partial, chunks, st->sms, s);
+  }
 }
 
 }  // extern "C"

@@ -28,7 +28,7 @@ EXPORTED = (
     "ps_normalize_workspace_bytes", "ps_normalize", "ps_gram", "ps_square", "ps_sym_product",
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
-    "ps_profile_enable", "ps_profile_read",
+    "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc",
 )
 
 
@@ -70,6 +70,8 @@ _SIGNATURES = {
     "ps_normalize_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "ps_normalize": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _i64, _i64,
                       _ptr, _i64, _ptr], _int),
+    "ps_normalize_noalloc": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _i64,
+                              _i64, _ptr], _int),
     "ps_gram": ([_ptr, _ptr, _i64, _i64, _i64, _i64, _ptr], _int),
     "ps_square": ([_ptr, _ptr, _ptr, _i64, _i64, _f32, _f32, _f32, _ptr], _int),
     "ps_sym_product": ([_ptr, _ptr, _ptr, _ptr, _i64, _i64, _f32, _f32, _f32, _ptr], _int),
