@@ -198,17 +198,79 @@ def config_dict(args, shapes, method):
             "parallelism": f"matrix-sharded x{args.gpus}, NCCL all-gather of FP16 updates"}
 
 
+def run_kernel(args):
+    """--kernel: time one kernel class alone on the workload's batched shapes
+    (also the small, self-contained command used for ncu captures)."""
+    from polar_switch import cuda_ops
+    from polar_switch import _native as nat
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    shapes = bank_shapes(args.workload)
+    g = torch.Generator(device=device).manual_seed(0)
+    if args.kernel in ("square", "sym_product"):
+        n = min(shapes[args.bank][1:])
+        L = args.L or sum(Lg for Lg, r, c in shapes if min(r, c) == n)
+        X = torch.randn(L, n, 2 * n, generator=g, device=device)
+        A = torch.empty(L, n, n, device=device, dtype=torch.float16)
+        cuda_ops.gram(cuda_ops.normalize(X, 1e-7), False, A)
+        C, out = A.clone(), torch.empty_like(A)
+        P2 = A.clone()
+        del X
+        torch.cuda.empty_cache()
+        fn = ((lambda: cuda_ops.square(A, C, out, 1.0, 0.5, 0.25)) if args.kernel == "square"
+              else (lambda: cuda_ops.sym_product(A, P2, C, out, 1.0, 0.5, 0.25)))
+        desc = f"{args.kernel} L={L} n={n}"
+    else:
+        L, r, c = shapes[args.bank]
+        L = args.L or L
+        X = cuda_ops.normalize(torch.randn(L, r, c, generator=g, device=device), 1e-7)
+        n = min(r, c)
+        B = torch.empty(L, n, n, device=device, dtype=torch.float16)
+        cuda_ops.gram(X, r > c, B)
+        if args.kernel == "gram":
+            fn = lambda: cuda_ops.gram(X, r > c, B)  # noqa: E731
+        elif args.kernel == "apply":
+            Y = torch.empty_like(X)
+            fn = lambda: cuda_ops.apply(X, B, r > c, 0.0, out=Y)  # noqa: E731
+        else:
+            X32 = torch.randn(L, r, c, generator=g, device=device)
+            Xh = torch.empty(L, r, c, device=device, dtype=torch.float16)
+            fn = lambda: cuda_ops.normalize(X32, 1e-7, out=Xh)  # noqa: E731
+        desc = f"{args.kernel} L={L} {r}x{c}"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    nat.profile_enable(True)
+    for _ in range(args.steps):
+        fn()
+    prof = nat.profile_read()
+    nat.profile_enable(False)
+    kind = {"square": "square", "sym_product": "square"}.get(args.kernel, args.kernel)
+    v = prof[kind]
+    ms = v["ms"] / max(v["launches"], 1)
+    print(json.dumps({"kernel": desc, "ms_per_launch": ms, "launches": v["launches"],
+                      "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12 if v["flops"] else None,
+                      "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="qwen", choices=sorted(WORKLOADS))
     ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize"],
+                    help="time one kernel class alone (for profiling) instead of the whole step")
+    ap.add_argument("--bank", type=int, default=0, help="bank of the workload used by --kernel")
+    ap.add_argument("--L", type=int, default=0, help="--kernel: override the number of matrices")
     args = ap.parse_args()
+    if args.kernel:
+        run_kernel(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
