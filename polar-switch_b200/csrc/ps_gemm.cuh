@@ -311,14 +311,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     constexpr int OB = OutTraits<OUT>::kBytes;
     constexpr int ROW_BYTES = 32 * OB;              // one staged row: 64 B or 128 B
-    constexpr int BUF_BYTES = 32 * ROW_BYTES;       // 32 x 32 sub-tile
-    constexpr int NBUF = EPI_WARP_BYTES / BUF_BYTES;
+    constexpr int BUF_BYTES = 32 * ROW_BYTES;       // one 32 x 32 sub-tile
+    // A slot holds what one chunk stores: the sub-tile, plus its transpose for
+    // symmetric products. Slots rotate; one bulk group per slot.
+    constexpr int SLOT_BYTES = SYM ? 2 * BUF_BYTES : BUF_BYTES;
+    constexpr int NSLOT = EPI_WARP_BYTES / SLOT_BYTES;
+    static_assert(NSLOT >= 2, "epilogue staging needs at least two slots");
     static_assert(!SYM || OUT == kOutF16, "symmetric products are stored in FP16");
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t stg = smem_u32(s_epi + (warp - 2) * EPI_WARP_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
-    int buf = 0;
+    int slot = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
       int b, m0, n0;
@@ -340,41 +344,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int cc = n0; cc < col_end; cc += 64) prefetch_l2(crow + cc);
         prefetch_l2(crow + col_end - 1);
       }
+      // Addend vectors of chunk c, loaded coalesced: vector k is row 8k + lane/4,
+      // columns 8 * (lane & 3) .. +7 of the warp's 32 x 32 sub-tile; they are
+      // transposed to one row per lane through the staging slot.
       auto load_addend = [&](int c, uint4 (&dst)[4]) {
-        const int g0 = n0 + 32 * c;
-        if (!load_c) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(0, 0, 0, 0);
-        } else if (g0 + 32 <= ncols_total) {
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(0, 0, 0, 0);
+        if (!args.has_addend) return;
+        const int gc = n0 + 32 * c + 8 * (lane & 3);
+        const __half* cbat = args.C + static_cast<long long>(b) * args.c_bs;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = ld_global_v4(crow + g0 + 8 * j);
-        } else {
-          __half* hv = reinterpret_cast<__half*>(dst);
-          for (int j = 0; j < 32; ++j)
-            hv[j] = (g0 + j < ncols_total) ? crow[g0 + j] : __float2half(0.f);
+        for (int k = 0; k < 4; ++k) {
+          const int gr = row0 + 8 * k + (lane >> 2);
+          if (gr >= args.M || gc >= ncols_total) continue;
+          const __half* src = cbat + static_cast<long long>(gr) * args.c_ld + gc;
+          if (gc + 8 <= ncols_total) {
+            dst[k] = ld_global_v4(src);
+          } else {
+            __half* hv = reinterpret_cast<__half*>(&dst[k]);
+            for (int e = 0; e < 8; ++e) hv[e] = (gc + e < ncols_total) ? src[e] : __float2half(0.f);
+          }
         }
       };
-      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, args.status,
-                             kStatusEpilogueTimeout, args.wait_limit)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint4 cv_next[4];
-      load_addend(0, cv_next);
-      for (int c = 0; c < nchunks; ++c) {
+      // Math, conversion and staging of chunk c (32 columns of this warp's
+      // 32 rows), then one bulk group with its TMA store(s).
+      auto process = [&](int c, const uint32_t (&v)[32], const uint4 (&av)[4]) {
         const int gcol0 = n0 + 32 * c;
-        // Addend of this chunk was loaded one chunk ahead; start the next one.
-        uint4 cv[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
-        if (c + 1 < nchunks) load_addend(c + 1, cv_next);
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
-                               static_cast<uint32_t>(acc * BN + 32 * c),
-                           v);
-        if (c == nchunks - 1) {
-          tc_fence_before();
+        if (lane == 0) bulk_wait_read<NSLOT - 1>();  // the slot's previous stores have read it
+        __syncwarp();
+        const uint32_t sb = stg + slot * SLOT_BYTES;
+        uint4 cv[4];
+        if (args.has_addend) {
+          // 64-byte FP16 rows, same swizzle as the output staging below
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int r = 8 * k + (lane >> 2), j = lane & 3;
+            st_shared_v4(sb + r * 64 + ((j ^ ((r >> 1) & 3)) << 4), av[k].x, av[k].y, av[k].z,
+                         av[k].w);
+          }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) cv[j] = ld_shared_v4(sb + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
         }
         float f[32];
         if (args.has_addend) {
@@ -394,49 +404,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         uint32_t w[32];
         convert_row<OUT>(f, w);
-
-        // -------- normal store of this 32x32 sub-tile
-        if (lane == 0) bulk_wait_read<NBUF - 1>();
-        __syncwarp();
-        {
-          const uint32_t sb = stg + buf * BUF_BYTES;
-          if (ROW_BYTES == 64) {
-            // 64-byte rows, TMA SWIZZLE_64B: 16 B chunk j -> j ^ ((row >> 1) & 3)
+        const bool mirror = SYM && (gcol0 / BM) != (m0 / BM);
+        // With 64-byte output rows each lane only overwrites the addend row it
+        // read itself; 128-byte output rows span other lanes' addend rows.
+        if (ROW_BYTES != 64 && args.has_addend) __syncwarp();
+        if (ROW_BYTES == 64) {
+          // 64-byte rows, TMA SWIZZLE_64B: 16 B chunk j -> j ^ ((row >> 1) & 3)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int p = j ^ ((lane >> 1) & 3);
-              st_shared_v4(sb + lane * 64 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
-                           w[4 * j + 3]);
-            }
-          } else {
-            // 128-byte rows, TMA SWIZZLE_128B: chunk j -> j ^ (row & 7)
+          for (int j = 0; j < 4; ++j) {
+            const int p = j ^ ((lane >> 1) & 3);
+            st_shared_v4(sb + lane * 64 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                         w[4 * j + 3]);
+          }
+        } else {
+          // 128-byte rows, TMA SWIZZLE_128B: chunk j -> j ^ (row & 7)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int p = j ^ (lane & 7);
-              st_shared_v4(sb + lane * 128 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
-                           w[4 * j + 3]);
-            }
+          for (int j = 0; j < 8; ++j) {
+            const int p = j ^ (lane & 7);
+            st_shared_v4(sb + lane * 128 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                         w[4 * j + 3]);
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (row0 < args.M && gcol0 < ncols_total) tma_store_3d(&tmD, sb, gcol0, row0, b);
-            bulk_commit();
-          }
-          buf = (buf + 1 == NBUF) ? 0 : buf + 1;
         }
-
-        // -------- mirrored store (symmetric, off the block diagonal)
-        if (SYM && (gcol0 / BM) != (m0 / BM)) {
-          if (lane == 0) bulk_wait_read<NBUF - 1>();
-          __syncwarp();
-          const uint32_t sb = stg + buf * BUF_BYTES;
+        if (mirror) {
           // Transposed sub-tile: row t = column of D, column = lane (row of D).
           // Lane pairs swap halves so each lane stores 4 bytes.
+          const uint32_t st = sb + BUF_BYTES;
           const int odd = lane & 1;
-          const int trow_base = odd;
-          const int tcol = lane & ~1;
-          const int cbyte = tcol * 2;
+          const int cbyte = (lane & ~1) * 2;
 #pragma unroll
           for (int p = 0; p < 16; ++p) {
             const uint32_t mine = w[p];
@@ -444,17 +438,67 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
             const uint32_t val = odd ? ((recv & 0xFFFFu) | (mine & 0xFFFF0000u))
                                      : ((mine & 0xFFFFu) | (recv << 16));
-            const int trow = 2 * p + trow_base;
-            const int chunk = (cbyte >> 4) ^ ((trow >> 1) & 3);
-            st_shared_u32(sb + trow * 64 + chunk * 16 + (cbyte & 15), val);
+            const int trow = 2 * p + odd;
+            const int ch = (cbyte >> 4) ^ ((trow >> 1) & 3);
+            st_shared_u32(st + trow * 64 + ch * 16 + (cbyte & 15), val);
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (gcol0 < ncols_total && row0 < args.M) tma_store_3d(&tmD, sb, row0, gcol0, b);
-            bulk_commit();
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < args.M && gcol0 < ncols_total) {
+            tma_store_3d(&tmD, sb, gcol0, row0, b);
+            if (mirror) tma_store_3d(&tmD, sb + BUF_BYTES, row0, gcol0, b);
           }
-          buf = (buf + 1 == NBUF) ? 0 : buf + 1;
+          bulk_commit();
+        }
+        slot = (slot + 1 == NSLOT) ? 0 : slot + 1;
+      };
+      // The accumulator may be reused as soon as every TMEM load has landed.
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      };
+
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, args.status,
+                             kStatusEpilogueTimeout, args.wait_limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
+      // TMEM loads run one chunk ahead of the math (two register sets), the
+      // addend loads one chunk ahead as well.
+      uint32_t va[32], vb[32];
+      uint4 cv_next[4];
+      load_addend(0, cv_next);
+      tmem_ld_32x32b_x32_async(tbase, va);
+      tmem_ld_wait_regs(va);
+      if (nchunks == 1) release();
+      for (int c = 0; c < nchunks; c += 2) {
+        uint4 cva[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+        const bool has_b = c + 1 < nchunks;
+        if (has_b) {
+          load_addend(c + 1, cv_next);
+          tmem_ld_32x32b_x32_async(tbase + 32 * (c + 1), vb);
+        }
+        process(c, va, cva);
+        if (has_b) {
+          tmem_ld_wait_regs(vb);
+          if (c + 1 == nchunks - 1) release();
+          uint4 cvb[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+          const bool has_a = c + 2 < nchunks;
+          if (has_a) {
+            load_addend(c + 2, cv_next);
+            tmem_ld_32x32b_x32_async(tbase + 32 * (c + 2), va);
+          }
+          process(c + 1, vb, cvb);
+          if (has_a) {
+            tmem_ld_wait_regs(va);
+            if (c + 2 == nchunks - 1) release();
+          }
         }
       }
       if (++acc == 2) {
