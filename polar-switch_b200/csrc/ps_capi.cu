@@ -16,6 +16,7 @@
 
 #include "../../include/polar_switch_b200.h"
 #include "ps_gemm.cuh"
+#include "ps_gemm2.cuh"
 #include "ps_norm.cuh"
 
 namespace ps {
@@ -47,6 +48,8 @@ enum ProfKind : int {
 
 thread_local std::string g_last_error;
 long long g_wait_limit = ps::kDefaultWaitLimit;
+// GEMMs run as CTA pairs (cta_group::2) unless switched off by ps_set_cta_pairs.
+bool g_use_pair = true;
 
 // Every kernel launch of the library is counted; when profiling is enabled,
 // each launch is also bracketed by CUDA events on its stream and tagged with
@@ -119,6 +122,8 @@ struct DeviceState {
   int sms = 0;
   int* status = nullptr;  // device address of ps::g_status on this device
   bool smem_attr[kNumVariants] = {};
+  bool pair_ready[kNumVariants] = {};
+  int pair_clusters[kNumVariants] = {};
 };
 
 std::mutex g_mu;
@@ -229,12 +234,89 @@ int map_out(CUtensorMap* m, const void* p, int dtype, int64_t cols, int64_t rows
   return make_map(m, p, dtype, cols, rows, L, ld, bs, 32, 32, sw);
 }
 
+// Rows of the B-operand box a K-major B tile needs in the selected kernel.
+uint32_t b_box_rows() { return g_use_pair ? ps::pair::BNH : ps::BN; }
+
+// Same problem as `g`, tiled for the CTA-pair kernel.
+ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
+  ps::pair::PairArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.M = g.M;
+  a.N = g.N;
+  a.K = g.K;
+  a.L = g.L;
+  a.alpha = g.alpha;
+  a.beta = g.beta;
+  a.diag = g.diag;
+  a.C = g.C;
+  a.c_ld = g.c_ld;
+  a.c_bs = g.c_bs;
+  a.has_addend = g.has_addend;
+  a.has_diag = g.has_diag;
+  if (sym) {
+    a.tb = (g.M + ps::pair::BM - 1) / ps::pair::BM;
+    const int P = (a.tb + 1) / 2;
+    a.tiles_per_mat = P * (P + 1) / 2;
+  } else {
+    a.tiles_m2 = (g.M + 2 * ps::pair::BM - 1) / (2 * ps::pair::BM);
+    a.tiles_n = (g.N + ps::pair::BN - 1) / ps::pair::BN;
+    a.group_m = a.tiles_m2 < 8 ? a.tiles_m2 : 8;
+    a.tiles_per_mat = a.tiles_m2 * a.tiles_n;
+  }
+  a.total_tiles = a.L * a.tiles_per_mat;
+  return a;
+}
+
+template <bool A_MN, bool B_MN, bool SYM, int OUT>
+int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const CUtensorMap& td, ps::pair::PairArgs args, cudaStream_t stream,
+                     DeviceState* st, int kind, double flops, double bytes) {
+  auto kern = ps::pair::ps_gemm_pair_kernel<A_MN, B_MN, SYM, OUT>;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.blockDim = dim3(ps::pair::NUM_THREADS);
+  cfg.dynamicSmemBytes = ps::pair::SMEM_TOTAL;
+  cfg.stream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  if (!st->pair_ready[variant]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         ps::pair::SMEM_TOTAL);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair gemm smem)");
+    cfg.gridDim = dim3(2 * (st->sms / 2));
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+    if (clusters < 1) return fail(PS_ERR_UNSUPPORTED, "no co-resident CTA pair fits on the device");
+    st->pair_clusters[variant] = clusters;
+    st->pair_ready[variant] = true;
+  }
+  if (args.total_tiles <= 0) return PS_OK;
+  args.status = st->status;
+  args.wait_limit = g_wait_limit;
+  const int pairs = args.total_tiles < st->pair_clusters[variant] ? args.total_tiles
+                                                                  : st->pair_clusters[variant];
+  cfg.gridDim = dim3(2 * pairs);
+  LaunchScope scope(kind, stream, flops, bytes);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, args);
+  if (e != cudaSuccess) return cuda_fail(e, "pair gemm launch");
+  return PS_OK;
+}
+
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
 int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                 ps::GemmArgs args, cudaStream_t stream, int kind, double flops, double bytes) {
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
+  if (g_use_pair)
+    return launch_gemm_pair<A_MN, B_MN, SYM, OUT>(variant, ta, tb, td, to_pair(args, SYM), stream,
+                                                  st, kind, flops, bytes);
   auto kern = ps::ps_gemm_kernel<A_MN, B_MN, SYM, OUT>;
   if (!st->smem_attr[variant]) {
     cudaError_t e =
@@ -308,7 +390,7 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   const bool same = p == q;
   if ((rc = map_kmajor(&ta, p, n, n, L, n, n * n, ps::BM))) return rc;
   if (same) {
-    if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, ps::BN))) return rc;
+    if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, b_box_rows()))) return rc;
   } else {
     if ((rc = map_mnmajor(&tb, q, n, n, L, n, n * n))) return rc;
   }
@@ -351,7 +433,7 @@ int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, i
   const double bytes = static_cast<double>(L) * 2.0 * (static_cast<double>(n) * K + n * n);
   if (!tall) {
     if ((rc = map_kmajor(&ta, x, K, n, L, x_ld, rows * x_ld, ps::BM))) return rc;
-    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, ps::BN))) return rc;
+    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, b_box_rows()))) return rc;
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfGram,
                                                         flops, bytes);
   }
@@ -694,6 +776,12 @@ int ps_profile_read(int kind, double* total_ms, int64_t* launches, double* flops
   *flops = f;
   *bytes = b;
   return PS_OK;
+}
+
+int ps_set_cta_pairs(int enable) {
+  const int previous = g_use_pair ? 1 : 0;
+  g_use_pair = enable != 0;
+  return previous;
 }
 
 int ps_set_wait_limit(long long cycles) {

@@ -1,0 +1,460 @@
+// CTA-pair (cta_group::2) version of the GEMM family of ps_gemm.cuh.
+//
+// Two CTAs of a cluster (an SM pair) compute one 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256): each CTA stages its own 128 rows
+// of A and its own half (128 columns) of B, the leader CTA issues the UMMAs,
+// and each CTA's TMEM receives its 128 x 256 accumulator. Against the 1-CTA
+// kernel this halves the B bytes each SM streams from L2 and shrinks a stage
+// to 32 KB, which leaves room for a 5-deep load ring and 8 epilogue warps
+// (two per TMEM lane quarter, each draining 128 of the 256 columns).
+//
+// Symmetric products use 128-row blocks as before: a pair tile covers block
+// rows 2q (leader) and 2q+1 (peer) against block columns 2p, 2p+1 for q <= p;
+// a CTA stores a block it computed only if it lies on or above the diagonal,
+// mirrored when strictly above (so each block pair still has one owner).
+//
+// Pipeline, per pair: both producers wait for their own free stage and load
+// into their own shared memory, counting bytes on the leader's full barrier
+// (the leader alone arms it with both CTAs' bytes); the leader's UMMA thread
+// frees a stage in both CTAs and announces an accumulator to both epilogues
+// with tcgen05.commit; all 16 epilogue warps release an accumulator on the
+// leader's barrier. Every wait is bounded as in ps_gemm.cuh. Loads fill only
+// the issuing CTA's own shared memory.
+#pragma once
+
+#include "ps_gemm.cuh"
+
+namespace ps {
+namespace pair {
+
+constexpr int BM = 128;                 // rows per CTA
+constexpr int BN = 256;                 // accumulator columns per CTA (pair N)
+constexpr int BNH = 128;                // B columns staged per CTA
+constexpr int BK = 64;
+constexpr int STAGES = 5;
+constexpr int UMMA_K = 16;
+constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_STAGE_BYTES = BNH * BK * 2;  // 16 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;  // 320
+constexpr int EPI_WARP_BYTES = 8192;
+constexpr int SMEM_OPERANDS = STAGES * STAGE_BYTES;
+constexpr int SMEM_EPI = NUM_EPI_WARPS * EPI_WARP_BYTES;
+constexpr int SMEM_CTRL = 256;
+constexpr int SMEM_TOTAL = SMEM_OPERANDS + SMEM_EPI + SMEM_CTRL + 1024;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+static_assert(SMEM_TOTAL <= 232448, "shared memory budget");
+
+struct PairArgs {
+  int M, N, K, L;
+  int tiles_m2, tiles_n;  // general: pair tiles (256 rows) x column tiles
+  int tb;                 // symmetric: 128-row blocks
+  int tiles_per_mat, total_tiles;
+  int group_m;            // general: pair-tile rows per rasterisation group
+  float alpha, beta, diag;
+  const __half* C;
+  long long c_ld, c_bs;
+  int has_addend, has_diag;
+  int* status;
+  long long wait_limit;
+};
+
+// Tile t of the pair -> batch b, this CTA's first row m0, the tile's first
+// column n0 (256 columns; this CTA stages B columns n0 + 128 * rank ...).
+template <bool SYM>
+__device__ __forceinline__ void decode(const PairArgs& a, int t, uint32_t rank, int& b, int& m0,
+                                       int& n0) {
+  b = t / a.tiles_per_mat;
+  int r = t - b * a.tiles_per_mat;
+  if (SYM) {
+    // column pair p owns row pairs 0..p
+    int p = 0;
+    while (r > p) {
+      r -= p + 1;
+      ++p;
+    }
+    m0 = (2 * r + static_cast<int>(rank)) * BM;
+    n0 = 2 * p * BM;
+  } else {
+    const int per_group = a.group_m * a.tiles_n;
+    const int g = r / per_group;
+    const int first = g * a.group_m;
+    const int gsz = min(a.group_m, a.tiles_m2 - first);
+    const int idx = r - g * per_group;
+    m0 = (first + idx % gsz) * (2 * BM) + static_cast<int>(rank) * BM;
+    n0 = (idx / gsz) * BN;
+  }
+}
+
+template <bool A_MN, bool B_MN, bool SYM, int OUT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    ps_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmD, const PairArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* s_epi = smem + SMEM_OPERANDS;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_epi + SMEM_EPI);
+  uint64_t* full = bars;                  // [STAGES] (used in the leader)
+  uint64_t* empty = bars + STAGES;        // [STAGES]
+  uint64_t* tfull = bars + 2 * STAGES;    // [2]
+  uint64_t* tempty = tfull + 2;           // [2]   (used in the leader)
+  uint64_t* drain = tempty + 2;           // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * NUM_EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_kb = (args.K + BK - 1) / BK;
+  const int ncols_total = args.N;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = pair_id; t < args.total_tiles && ok; t += npairs) {
+        int b, m0, n0;
+        decode<SYM>(args, t, rank, b, m0, n0);
+        const int nb = n0 + static_cast<int>(rank) * BNH;  // this CTA's half of B
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status,
+                                 kStatusProducerTimeout, args.wait_limit)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + stage * STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_STAGE_BYTES;
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_3d_pair(&tmA, a_dst, bar, k0, m0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_3d_pair(&tmA, a_dst + j * MN_ATOM_BYTES, bar, m0 + 64 * j, k0, b);
+          }
+          if (!B_MN) {
+            tma_load_3d_pair(&tmB, b_dst, bar, k0, nb, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BNH / 64; ++j)
+              tma_load_3d_pair(&tmB, b_dst + j * MN_ATOM_BYTES, bar, nb + 64 * j, k0, b);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Tail: every stage this CTA filled must have been released by the
+      // leader's UMMAs (their commits arrive on this CTA's barriers) before
+      // either CTA may exit.
+      for (int s = 0; s < STAGES; ++s) {
+        if (!(issued_mask & (1u << s))) continue;
+        const uint32_t par = (issued_parity >> s) & 1u;
+        const long long start = clock64();
+        while (!mbar_try_wait(&empty[s], par)) {
+          if (clock64() - start > args.wait_limit) {
+            if (args.status) atomicCAS(args.status, 0, kStatusDrainTimeout);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer (leader)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      const uint32_t idesc = make_idesc_f16(2 * BM, BN, A_MN, B_MN);
+      const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), peer);
+      const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), peer);
+      for (int t = pair_id; t < args.total_tiles && ok; t += npairs) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status,
+                               kStatusMmaTimeout, args.wait_limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.status, kStatusMmaTimeout,
+                                 args.wait_limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t ad = A_MN ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
+                                                            MN_ATOM_BYTES, 1024)
+                                     : make_smem_desc_sw128(a_addr + kk * (UMMA_K * 2), 16, 1024);
+            const uint64_t bd = B_MN ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
+                                                            MN_ATOM_BYTES, 1024)
+                                     : make_smem_desc_sw128(b_addr + kk * (UMMA_K * 2), 16, 1024);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          // free this stage in both CTAs
+          umma_commit_pair(smem_u32(&empty[stage]));
+          umma_commit_pair(empty_peer0 + stage * 8);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[acc]));
+        umma_commit_pair(tfull_peer0 + acc * 8);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        umma_commit_pair(smem_u32(drain));
+        const long long start = clock64();
+        while (!mbar_try_wait(drain, 0)) {
+          if (clock64() - start > args.wait_limit) {
+            if (args.status) atomicCAS(args.status, 0, kStatusDrainTimeout);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    constexpr int OB = OutTraits<OUT>::kBytes;
+    constexpr int ROW_BYTES = 32 * OB;
+    constexpr int BUF_BYTES = 32 * ROW_BYTES;
+    constexpr int SLOT_BYTES = SYM ? 2 * BUF_BYTES : BUF_BYTES;
+    constexpr int NSLOT = EPI_WARP_BYTES / SLOT_BYTES;
+    static_assert(NSLOT >= 2, "epilogue staging needs at least two slots");
+    static_assert(!SYM || OUT == kOutF16, "symmetric products are stored in FP16");
+    const int q = warp & 3;               // TMEM lane quarter
+    const int h = (warp - 2) >> 2;        // column half of the 256-column accumulator
+    const uint32_t stg = smem_u32(s_epi + (warp - 2) * EPI_WARP_BYTES);
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int slot = 0;
+    bool ok = true;
+    for (int t = pair_id; t < args.total_tiles && ok; t += npairs) {
+      int b, m0, n0;
+      decode<SYM>(args, t, rank, b, m0, n0);
+      const int c_first = 4 * h;            // this warp's chunks: c_first .. c_first + 3
+      int nvalid = ncols_total - (n0 + 32 * c_first);
+      nvalid = nvalid > 128 ? 128 : nvalid;
+      const int nchunks = nvalid > 0 ? (nvalid + 31) >> 5 : 0;
+      const int row0 = m0 + 32 * q;
+      const int grow = row0 + lane;
+      // symmetric: skip blocks below the diagonal (another CTA owns their pair)
+      const int blk_col = (n0 + 32 * c_first) / BM;
+      const bool skip_block = SYM && (m0 / BM) > blk_col;
+      const bool work = nchunks > 0 && !skip_block && row0 < args.M;
+      const bool row_ok = grow < args.M;
+      const bool load_c = work && args.has_addend && row_ok;
+      const __half* crow =
+          args.has_addend ? args.C + static_cast<long long>(b) * args.c_bs +
+                                static_cast<long long>(grow) * args.c_ld
+                          : nullptr;
+      if (load_c) {
+        const int cb = n0 + 32 * c_first;
+        const int ce = min(cb + nvalid, ncols_total);
+        for (int cc = cb; cc < ce; cc += 64) prefetch_l2(crow + cc);
+        prefetch_l2(crow + ce - 1);
+      }
+      auto load_addend = [&](int c, uint4 (&dst)[4]) {
+        const int g0 = n0 + 32 * c;
+        if (!load_c) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(0, 0, 0, 0);
+        } else if (g0 + 32 <= ncols_total) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = ld_global_v4(crow + g0 + 8 * j);
+        } else {
+          __half* hv = reinterpret_cast<__half*>(dst);
+          for (int j = 0; j < 32; ++j)
+            hv[j] = (g0 + j < ncols_total) ? crow[g0 + j] : __float2half(0.f);
+        }
+      };
+      auto process = [&](int c, const uint32_t (&v)[32], const uint4 (&cv)[4]) {
+        const int gcol0 = n0 + 32 * c;
+        float f[32];
+        if (args.has_addend) {
+          const __half* hv = reinterpret_cast<const __half*>(cv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            f[j] = fmaf(args.beta, __half2float(hv[j]), args.alpha * __uint_as_float(v[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = args.alpha * __uint_as_float(v[j]);
+        }
+        if (SYM && args.has_diag) {
+          const int d = grow - gcol0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j == d) f[j] += args.diag;
+        }
+        uint32_t w[32];
+        convert_row<OUT>(f, w);
+        const bool mirror = SYM && (gcol0 / BM) != (m0 / BM);
+        if (lane == 0) bulk_wait_read<NSLOT - 1>();
+        __syncwarp();
+        const uint32_t sb = stg + slot * SLOT_BYTES;
+        if (ROW_BYTES == 64) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int p = j ^ ((lane >> 1) & 3);
+            st_shared_v4(sb + lane * 64 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                         w[4 * j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int p = j ^ (lane & 7);
+            st_shared_v4(sb + lane * 128 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                         w[4 * j + 3]);
+          }
+        }
+        if (mirror) {
+          const uint32_t st = sb + BUF_BYTES;
+          const int odd = lane & 1;
+          const int cbyte = (lane & ~1) * 2;
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const uint32_t mine = w[p];
+            const uint32_t send = odd ? (mine & 0xFFFFu) : (mine >> 16);
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const uint32_t val = odd ? ((recv & 0xFFFFu) | (mine & 0xFFFF0000u))
+                                     : ((mine & 0xFFFFu) | (recv << 16));
+            const int trow = 2 * p + odd;
+            const int ch = (cbyte >> 4) ^ ((trow >> 1) & 3);
+            st_shared_u32(st + trow * 64 + ch * 16 + (cbyte & 15), val);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < args.M && gcol0 < ncols_total) {
+            tma_store_3d(&tmD, sb, gcol0, row0, b);
+            if (mirror) tma_store_3d(&tmD, sb + BUF_BYTES, row0, gcol0, b);
+          }
+          bulk_commit();
+        }
+        slot = (slot + 1 == NSLOT) ? 0 : slot + 1;
+      };
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+      };
+
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, args.status,
+                             kStatusEpilogueTimeout, args.wait_limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (!work) {
+        release();
+      } else {
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                               static_cast<uint32_t>(acc * BN + 32 * c_first);
+        uint32_t va[32], vb[32];
+        uint4 cv_next[4];
+        load_addend(c_first, cv_next);
+        tmem_ld_32x32b_x32_async(tbase, va);
+        tmem_ld_wait_regs(va);
+        if (nchunks == 1) release();
+        for (int i = 0; i < nchunks; i += 2) {
+          const int c = c_first + i;
+          uint4 cva[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+          const bool has_b = i + 1 < nchunks;
+          if (has_b) {
+            load_addend(c + 1, cv_next);
+            tmem_ld_32x32b_x32_async(tbase + 32 * (i + 1), vb);
+          }
+          process(c, va, cva);
+          if (has_b) {
+            tmem_ld_wait_regs(vb);
+            if (i + 1 == nchunks - 1) release();
+            uint4 cvb[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+            const bool has_a = i + 2 < nchunks;
+            if (has_a) {
+              load_addend(c + 2, cv_next);
+              tmem_ld_32x32b_x32_async(tbase + 32 * (i + 2), va);
+            }
+            process(c + 1, vb, cvb);
+            if (has_a) {
+              tmem_ld_wait_regs(va);
+              if (i + 2 == nchunks - 1) release();
+            }
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still touch it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
+}  // namespace pair
+}  // namespace ps

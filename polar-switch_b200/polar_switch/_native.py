@@ -28,7 +28,7 @@ EXPORTED = (
     "ps_normalize_workspace_bytes", "ps_normalize", "ps_gram", "ps_square", "ps_sym_product",
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
-    "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc",
+    "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs",
 )
 
 
@@ -82,6 +82,7 @@ _SIGNATURES = {
                     ctypes.POINTER(_f32), ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep),
                     _int, _f32, _ptr, _i64, _ptr], _int),
     "ps_launch_count": ([], ctypes.c_longlong),
+    "ps_set_cta_pairs": ([_int], _int),
     "ps_profile_enable": ([_int], _int),
     "ps_profile_read": ([_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64),
                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], _int),
@@ -167,3 +168,8 @@ def profile_read():
                                                      ctypes.byref(fl), ctypes.byref(by)))
         out[name] = dict(ms=ms.value, launches=n.value, flops=fl.value, bytes=by.value)
     return out
+
+
+def set_cta_pairs(enable):
+    """Select the CTA-pair GEMM kernel (True, default) or the one-CTA kernel; returns the previous."""
+    return bool(load().ps_set_cta_pairs(1 if enable else 0))
