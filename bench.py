@@ -59,6 +59,13 @@ def make_banks(shapes, device, seed=0, scale=1.0):
             for L, r, c in shapes]
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per matrix of the
+# dominant kernel, from one ncu capture (profiles/ps_gemm_pair_square_qwen_n1024.md:
+# 308.2 MB for a launch over 64 matrices of n = 1024); scaled to a launch by its
+# number of matrices.
+TRAFFIC_BYTES_PER_MATRIX = {("square", 1024): 308.2e6 / 64}
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle-reason samples during the timed region."""
 
@@ -369,6 +376,11 @@ def main():
         gemm_kinds = {k: v for k, v in prof.items() if k in ("gram", "square", "apply") and v["launches"]}
         dom_name, dom = max(gemm_kinds.items(), key=lambda kv: kv[1]["ms"])
         achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
+        traffic = None
+        n_dom = min(min(r, c) for _, r, c in shapes)
+        if (dom_name, n_dom) in TRAFFIC_BYTES_PER_MATRIX and dom["launches"]:
+            mats_per_launch = dom["flops"] / dom["launches"] / float(n_dom) ** 3
+            traffic = TRAFFIC_BYTES_PER_MATRIX[(dom_name, n_dom)] * mats_per_launch
         peak = peaks.get("bf16_tflops_sustained")
         peak_src = "measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
         if peak is None:
@@ -385,7 +397,8 @@ def main():
             "config": config_dict(args, shapes, method),
             "roofline": {"bound": "tensor", "kernel": f"ps_gemm ({dom_name})", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": peak_src, "traffic": None,
+                         "peak_source": peak_src, "traffic": traffic,
+                         "traffic_source": "ncu dram read+write bytes per launch (profiles/)" if traffic else None,
                          "launches_per_step": dom["launches"] / args.steps},
             "kernels": breakdown,
             "cpu_baseline": cpu_baseline,
