@@ -89,9 +89,9 @@ PS_API int ps_profile_enable(int enable);
 PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double* flops,
                            double* bytes);
 
-/* Selects the GEMM kernel for later launches: 1 (default) = CTA-pair kernel
- * (tcgen05 cta_group::2, 256 x 256 tiles over two SMs), 0 = one-CTA kernel
- * (128 x 256 tiles). Both compute the same products with the same rounding.
+/* Selects the GEMM kernel for later launches: 0 (default) = one-CTA kernel
+ * (128 x 256 tiles), 1 = CTA-pair kernel (tcgen05 cta_group::2, 256 x 256
+ * tiles over two SMs). Both compute the same products with the same rounding.
  * Returns the previous setting. */
 PS_API int ps_set_cta_pairs(int enable);
 

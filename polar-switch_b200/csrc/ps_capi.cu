@@ -48,8 +48,9 @@ enum ProfKind : int {
 
 thread_local std::string g_last_error;
 long long g_wait_limit = ps::kDefaultWaitLimit;
-// GEMMs run as CTA pairs (cta_group::2) unless switched off by ps_set_cta_pairs.
-bool g_use_pair = true;
+// GEMMs run on the one-CTA kernel unless CTA pairs (cta_group::2) are selected
+// with ps_set_cta_pairs; measured faster on every circuit shape.
+bool g_use_pair = false;
 
 // Every kernel launch of the library is counted; when profiling is enabled,
 // each launch is also bracketed by CUDA events on its stream and tagged with
@@ -253,6 +254,9 @@ ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
   a.c_bs = g.c_bs;
   a.has_addend = g.has_addend;
   a.has_diag = g.has_diag;
+  a.a_tri = g.a_tri;
+  a.b_tri = g.b_tri;
+  a.store_mirror = g.store_mirror;
   if (sym) {
     a.tb = (g.M + ps::pair::BM - 1) / ps::pair::BM;
     const int P = (a.tb + 1) / 2;
@@ -268,9 +272,10 @@ ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
 }
 
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
-int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const CUtensorMap& td, ps::pair::PairArgs args, cudaStream_t stream,
-                     DeviceState* st, int kind, double flops, double bytes) {
+int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& ta2,
+                     const CUtensorMap& tb, const CUtensorMap& tb2, const CUtensorMap& td,
+                     ps::pair::PairArgs args, cudaStream_t stream, DeviceState* st, int kind,
+                     double flops, double bytes) {
   auto kern = ps::pair::ps_gemm_pair_kernel<A_MN, B_MN, SYM, OUT>;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -303,20 +308,27 @@ int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& tb,
                                                                   : st->pair_clusters[variant];
   cfg.gridDim = dim3(2 * pairs);
   LaunchScope scope(kind, stream, flops, bytes);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, args);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, ta2, tb, tb2, td, args);
   if (e != cudaSuccess) return cuda_fail(e, "pair gemm launch");
   return PS_OK;
 }
 
+// ta2 / tb2: the operands' maps in the other majorness, read only when the
+// operand is triangle-stored (args.a_tri / b_tri, CTA-pair kernel only).
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
 int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                ps::GemmArgs args, cudaStream_t stream, int kind, double flops, double bytes) {
+                ps::GemmArgs args, cudaStream_t stream, int kind, double flops, double bytes,
+                const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
+  if ((args.a_tri && !ta2) || (args.b_tri && !tb2))
+    return fail(PS_ERR_INVALID, "internal: triangle-stored operand without its second map");
   if (g_use_pair)
-    return launch_gemm_pair<A_MN, B_MN, SYM, OUT>(variant, ta, tb, td, to_pair(args, SYM), stream,
+    return launch_gemm_pair<A_MN, B_MN, SYM, OUT>(variant, ta, ta2 ? *ta2 : ta, tb,
+                                                  tb2 ? *tb2 : tb, td, to_pair(args, SYM), stream,
                                                   st, kind, flops, bytes);
+
   auto kern = ps::ps_gemm_kernel<A_MN, B_MN, SYM, OUT>;
   if (!st->smem_attr[variant]) {
     cudaError_t e =
@@ -329,7 +341,8 @@ int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const
   args.wait_limit = g_wait_limit;
   const int grid = args.total_tiles < st->sms ? args.total_tiles : st->sms;
   LaunchScope scope(kind, stream, flops, bytes);
-  kern<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(ta, tb, td, args);
+  kern<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(ta, ta2 ? *ta2 : ta, tb,
+                                                           tb2 ? *tb2 : tb, td, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return PS_OK;
@@ -362,6 +375,7 @@ ps::GemmArgs base_args(int64_t M, int64_t N, int64_t K, int64_t L) {
   a.K = static_cast<int>(K);
   a.L = static_cast<int>(L);
   a.alpha = 1.f;
+  a.store_mirror = 1;
   return a;
 }
 
@@ -373,7 +387,7 @@ bool dims_ok(int64_t L, int64_t r, int64_t c) {
 // ------------------------------------------------------------------ ops
 int sym_product_impl(const void* p, const void* q, const void* c, void* out, int64_t L,
                      int64_t n, float alpha, float beta, float diag, cudaStream_t stream,
-                     const char* name) {
+                     const char* name, bool tri = false) {
   if (!p || !q || !out) return fail(PS_ERR_INVALID, "%s: null pointer", name);
   if (!dims_ok(L, n, n)) return fail(PS_ERR_INVALID, "%s: bad sizes", name);
   if (n % 8) return fail(PS_ERR_INVALID, "%s: n=%lld must be a multiple of 8", name, (long long)n);
@@ -407,6 +421,15 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   a.has_diag = diag != 0.f;
   const double nn = static_cast<double>(n) * n;
   const double bytes = L * nn * 2.0 * ((same ? 1 : 2) + (c ? 1 : 0) + 1);
+  if (same && tri) {
+    // squared operand and result both held as upper-triangle blocks
+    CUtensorMap tm;
+    if ((rc = map_mnmajor(&tm, p, n, n, L, n, n * n))) return rc;
+    a.a_tri = a.b_tri = 1;
+    a.store_mirror = 0;
+    return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
+                                                        L * nn * n, bytes, &tm, &tm);
+  }
   if (same)
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
                                                         L * nn * n, bytes);
@@ -415,7 +438,7 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
 }
 
 int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
-              bool tall, cudaStream_t stream) {
+              bool tall, cudaStream_t stream, bool tri_out = false) {
   if (!x || !out) return fail(PS_ERR_INVALID, "ps_gram: null pointer");
   if (!dims_ok(L, rows, cols) || x_ld < cols)
     return fail(PS_ERR_INVALID, "ps_gram: bad sizes");
@@ -429,6 +452,7 @@ int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, i
   if ((rc = map_out(&td, out, PS_F16, n, n, L, n, n * n))) return rc;
   ps::GemmArgs a = base_args(n, n, K, L);
   fill_sym_tiles(a, n, L);
+  a.store_mirror = tri_out ? 0 : 1;
   const double flops = static_cast<double>(L) * n * n * K;
   const double bytes = static_cast<double>(L) * 2.0 * (static_cast<double>(n) * K + n * n);
   if (!tall) {
@@ -444,18 +468,19 @@ int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, i
 
 template <int OUT>
 int apply_launch(bool tall, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                 const ps::GemmArgs& a, cudaStream_t s) {
+                 const ps::GemmArgs& a, cudaStream_t s, const CUtensorMap* t2) {
   const double M = a.M, N = a.N, K = a.K, L = a.L;
   const double out_bytes = OUT == ps::kOutF32 ? 4.0 : 2.0;
   const double flops = 2.0 * L * M * N * K;
   const double bytes = L * (2.0 * K * K + 2.0 * M * N + out_bytes * M * N);
   (void)tall;  // both orientations are A (K-major) times B (MN-major)
-  return launch_gemm<false, true, false, OUT>(2 + OUT, ta, tb, td, a, s, kProfApply, flops, bytes);
+  return launch_gemm<false, true, false, OUT>(2 + OUT, ta, tb, td, a, s, kProfApply, flops, bytes,
+                                              a.a_tri ? t2 : nullptr, a.b_tri ? t2 : nullptr);
 }
 
 int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
                int64_t x_ld, float residual, int y_dtype, int64_t y_ld, bool tall,
-               cudaStream_t stream) {
+               cudaStream_t stream, bool tri_b = false) {
   if (!b || !x || !y) return fail(PS_ERR_INVALID, "ps_apply: null pointer");
   if (!dims_ok(L, rows, cols) || x_ld < cols || y_ld < cols)
     return fail(PS_ERR_INVALID, "ps_apply: bad sizes");
@@ -489,13 +514,24 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
     a.c_ld = x_ld;
     a.c_bs = rows * x_ld;
   }
+  // b held as upper-triangle blocks: its second map has the other majorness
+  CUtensorMap t2;
+  if (tri_b) {
+    if (!tall) {
+      if ((rc = map_mnmajor(&t2, b, n, n, L, n, n * n))) return rc;
+      a.a_tri = 1;
+    } else {
+      if ((rc = map_kmajor(&t2, b, n, n, L, n, n * n, b_box_rows()))) return rc;
+      a.b_tri = 1;
+    }
+  }
   switch (y_dtype) {
     case PS_F16:
-      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream);
+      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream, &t2);
     case PS_F32:
-      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream);
+      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream, &t2);
     default:
-      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream);
+      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream, &t2);
   }
 }
 
@@ -915,6 +951,9 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
   };
   std::vector<int> cur(np, 0);
   std::vector<bool> direct(np);
+  // Square buffers live only inside this call, so they are kept as
+  // upper-triangle blocks (no mirrored stores).
+  const bool tri = true;
   for (int i = 0; i < np; ++i) {
     const ps_problem& q = probs[i];
     const GroupedPlan::Prob& p = plan.probs[i];
@@ -932,7 +971,7 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
     for (int i = 0; i < np; ++i) {
       const GroupedPlan::Prob& p = plan.probs[i];
       if ((rc = gram_impl(ws + p.xh_off[cur[i]], buf_ptr(i, 0), probs[i].L, p.lay.Rp, p.lay.Cp,
-                          p.lay.Cp, p.lay.tall, s)))
+                          p.lay.Cp, p.lay.tall, s, tri)))
         return rc;
     }
     int last = 0;
@@ -943,7 +982,7 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
         uint8_t* base = ws + g.buf_off;
         if ((rc = sym_product_impl(base + q.src * g.buf_bytes, base + q.src * g.buf_bytes,
                                    base + q.add * g.buf_bytes, base + q.dst * g.buf_bytes, g.Ltot,
-                                   g.n, q.alpha, q.beta, q.diag, s, "ps_circuit(square)")))
+                                   g.n, q.alpha, q.beta, q.diag, s, "ps_circuit(square)", tri)))
           return rc;
       }
       last = q.dst;
@@ -956,10 +995,10 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
       const int64_t Rp = p.lay.Rp, Cp = p.lay.Cp;
       if (final_iter && direct[i]) {
         rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], q.y, q.L, Rp, Cp, Cp,
-                        residuals[t], q.y_dtype, q.cols, p.lay.tall, s);
+                        residuals[t], q.y_dtype, q.cols, p.lay.tall, s, tri);
       } else {
         rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], ws + p.xh_off[1 - cur[i]], q.L,
-                        Rp, Cp, Cp, residuals[t], PS_F16, Cp, p.lay.tall, s);
+                        Rp, Cp, Cp, residuals[t], PS_F16, Cp, p.lay.tall, s, tri);
         cur[i] = 1 - cur[i];
       }
       if (rc) return rc;

@@ -43,9 +43,9 @@ constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int MN_ATOM_BYTES = 64 * BK * 2;  // one 64(MN) x 64(K) MN-major box: 8 KB
-constexpr int NUM_EPI_WARPS = 4;
+constexpr int NUM_EPI_WARPS = 8;   // two per TMEM lane quarter, 128 columns each
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
-constexpr int EPI_WARP_BYTES = 8192;
+constexpr int EPI_WARP_BYTES = 4096;
 constexpr int SMEM_OPERANDS = STAGES * STAGE_BYTES;
 constexpr int SMEM_EPI = NUM_EPI_WARPS * EPI_WARP_BYTES;
 constexpr int SMEM_CTRL = 256;
@@ -65,6 +65,9 @@ struct GemmArgs {
   const __half* C;           // addend (FP16), may alias D in symmetric mode
   long long c_ld, c_bs;      // addend leading dimension / batch stride (elements)
   int has_addend, has_diag;
+  // Triangle storage, honoured by the CTA-pair kernel only (see ps_gemm2.cuh);
+  // this kernel always stores full symmetric results.
+  int a_tri, b_tri, store_mirror;
   int* status;               // device status word
   long long wait_limit;      // cycles before a bounded wait gives up
 };
@@ -93,6 +96,18 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& b, in
     m0 = (first + idx % gsz) * BM;
     n0 = (idx / gsz) * BN;
   }
+}
+
+// Triangle storage: a symmetric operand may be held as its 128x128 blocks on
+// and above the diagonal only. For an operand tile whose 128-row blocks are
+// lo..hi, k-block kb (a 128-wide block index) must then be read from the
+// stored transposed block with the other majorness. K-native tiles hold rows
+// of the operand (element (r, k) stored iff block(r) <= kb), MN-native tiles
+// hold its columns. When a tile switches, a diagonal block it covers is read
+// transposed too, which is exact: diagonal blocks are bit-symmetric (both
+// triangles are computed by the same UMMA sums in the same order).
+__device__ __forceinline__ bool tri_transposed(bool mn_native, int lo, int hi, int kb) {
+  return mn_native ? (kb > lo) : (hi > kb);
 }
 
 template <int OUT>
@@ -133,8 +148,11 @@ __device__ __forceinline__ void convert_row(const float (&f)[32], uint32_t (&w)[
 
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    ps_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    ps_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB2,
                    const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
+  // tmA / tmB: boxes in the operand's native majorness (A_MN / B_MN);
+  // tmA2 / tmB2: the other majorness, read only for triangle-stored operands.
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms.
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -169,6 +187,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmD);
+    if (args.a_tri) tma_prefetch_desc(&tmA2);
+    if (args.b_tri) tma_prefetch_desc(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -202,19 +222,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* b_dst = a_dst + A_STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           const int k0 = kb * BK;
-          if (!A_MN) {
-            tma_load_3d(&tmA, a_dst, &full[stage], k0, m0, b);
+          const int kb128 = k0 / BM;
+          const bool at = args.a_tri && tri_transposed(A_MN, m0 / BM, m0 / BM, kb128);
+          const bool bt = args.b_tri && tri_transposed(B_MN, n0 / BM, n0 / BM + 1, kb128);
+          const CUtensorMap* ma = at ? &tmA2 : &tmA;
+          const CUtensorMap* mb = bt ? &tmB2 : &tmB;
+          if (A_MN == at) {  // K-major tile
+            tma_load_3d(ma, a_dst, &full[stage], k0, m0, b);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
-              tma_load_3d(&tmA, a_dst + j * MN_ATOM_BYTES, &full[stage], m0 + 64 * j, k0, b);
+              tma_load_3d(ma, a_dst + j * MN_ATOM_BYTES, &full[stage], m0 + 64 * j, k0, b);
           }
-          if (!B_MN) {
-            tma_load_3d(&tmB, b_dst, &full[stage], k0, n0, b);
+          if (B_MN == bt) {
+            tma_load_3d(mb, b_dst, &full[stage], k0, n0, b);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(&tmB, b_dst + j * MN_ATOM_BYTES, &full[stage], n0 + 64 * j, k0, b);
+              tma_load_3d(mb, b_dst + j * MN_ATOM_BYTES, &full[stage], n0 + 64 * j, k0, b);
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -254,7 +279,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int nvalid = ncols_total - n0;
         nvalid = nvalid > BN ? BN : nvalid;
         const int n_mma = (nvalid + 15) & ~15;
-        const uint32_t idesc = make_idesc_f16(BM, n_mma, A_MN, B_MN);
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status,
                                kStatusMmaTimeout, args.wait_limit)) {
           ok = false;
@@ -271,12 +295,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_STAGE_BYTES;
+          const int kb128 = (kb * BK) / BM;
+          const bool a_mn = A_MN != (args.a_tri && tri_transposed(A_MN, m0 / BM, m0 / BM, kb128));
+          const bool b_mn =
+              B_MN != (args.b_tri && tri_transposed(B_MN, n0 / BM, n0 / BM + 1, kb128));
+          const uint32_t idesc = make_idesc_f16(BM, n_mma, a_mn, b_mn);
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint64_t ad = A_MN ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
+            const uint64_t ad = a_mn ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
                                                             MN_ATOM_BYTES, 1024)
                                      : make_smem_desc_sw128(a_addr + kk * (UMMA_K * 2), 16, 1024);
-            const uint64_t bd = B_MN ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
+            const uint64_t bd = b_mn ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
                                                             MN_ATOM_BYTES, 1024)
                                      : make_smem_desc_sw128(b_addr + kk * (UMMA_K * 2), 16, 1024);
             umma_f16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
@@ -316,9 +345,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // symmetric products. Slots rotate; one bulk group per slot.
     constexpr int SLOT_BYTES = SYM ? 2 * BUF_BYTES : BUF_BYTES;
     constexpr int NSLOT = EPI_WARP_BYTES / SLOT_BYTES;
-    static_assert(NSLOT >= 2, "epilogue staging needs at least two slots");
+    static_assert(NSLOT >= 1, "epilogue staging needs a slot");
     static_assert(!SYM || OUT == kOutF16, "symmetric products are stored in FP16");
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;         // TMEM lane quarter this warp may access
+    const int h = (warp - 2) >> 2;  // which 128 of the tile's 256 columns it drains
     const uint32_t stg = smem_u32(s_epi + (warp - 2) * EPI_WARP_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -327,9 +357,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
       int b, m0, n0;
       decode_tile<SYM>(args, t, b, m0, n0);
-      int nvalid = ncols_total - n0;
-      nvalid = nvalid > BN ? BN : nvalid;
-      const int nchunks = (nvalid + 31) >> 5;
+      const int c_first = 4 * h;  // this warp's chunks: c_first .. c_first + 3
+      int nvalid = ncols_total - (n0 + 32 * c_first);
+      nvalid = nvalid > BN / 2 ? BN / 2 : nvalid;
+      const int nchunks = nvalid > 0 ? (nvalid + 31) >> 5 : 0;
       const int row0 = m0 + 32 * q;       // first row of this warp's 32-row slab
       const int grow = row0 + lane;       // this thread's output row
       const bool row_ok = grow < args.M;
@@ -338,11 +369,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           args.has_addend ? args.C + static_cast<long long>(b) * args.c_bs +
                                 static_cast<long long>(grow) * args.c_ld
                           : nullptr;
-      const int col_end = min(n0 + nvalid, ncols_total);
       // Pull this thread's addend row into L2 while the UMMAs of the tile run.
-      if (load_c) {
-        for (int cc = n0; cc < col_end; cc += 64) prefetch_l2(crow + cc);
-        prefetch_l2(crow + col_end - 1);
+      if (load_c && nchunks > 0) {
+        const int cb = n0 + 32 * c_first;
+        const int ce = min(cb + nvalid, ncols_total);
+        for (int cc = cb; cc < ce; cc += 64) prefetch_l2(crow + cc);
+        prefetch_l2(crow + ce - 1);
       }
       // Addend vectors of chunk c, loaded coalesced: vector k is row 8k + lane/4,
       // columns 8 * (lane & 3) .. +7 of the warp's 32 x 32 sub-tile; they are
@@ -404,7 +436,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         uint32_t w[32];
         convert_row<OUT>(f, w);
-        const bool mirror = SYM && (gcol0 / BM) != (m0 / BM);
+        const bool mirror = SYM && args.store_mirror && (gcol0 / BM) != (m0 / BM);
         // With 64-byte output rows each lane only overwrites the addend row it
         // read itself; 128-byte output rows span other lanes' addend rows.
         if (ROW_BYTES != 64 && args.has_addend) __syncwarp();
@@ -467,37 +499,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
-      // TMEM loads run one chunk ahead of the math (two register sets), the
-      // addend loads one chunk ahead as well.
-      uint32_t va[32], vb[32];
-      uint4 cv_next[4];
-      load_addend(0, cv_next);
-      tmem_ld_32x32b_x32_async(tbase, va);
-      tmem_ld_wait_regs(va);
-      if (nchunks == 1) release();
-      for (int c = 0; c < nchunks; c += 2) {
-        uint4 cva[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
-        const bool has_b = c + 1 < nchunks;
-        if (has_b) {
-          load_addend(c + 1, cv_next);
-          tmem_ld_32x32b_x32_async(tbase + 32 * (c + 1), vb);
-        }
-        process(c, va, cva);
-        if (has_b) {
-          tmem_ld_wait_regs(vb);
-          if (c + 1 == nchunks - 1) release();
-          uint4 cvb[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
-          const bool has_a = c + 2 < nchunks;
-          if (has_a) {
-            load_addend(c + 2, cv_next);
-            tmem_ld_32x32b_x32_async(tbase + 32 * (c + 2), va);
+      if (nchunks == 0) {
+        release();
+      } else {
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                               static_cast<uint32_t>(acc * BN + 32 * c_first);
+        // TMEM loads run one chunk ahead of the math (two register sets), the
+        // addend loads one chunk ahead as well.
+        uint32_t va[32], vb[32];
+        uint4 cv_next[4];
+        load_addend(c_first, cv_next);
+        tmem_ld_32x32b_x32_async(tbase, va);
+        tmem_ld_wait_regs(va);
+        if (nchunks == 1) release();
+        for (int i = 0; i < nchunks; i += 2) {
+          const int c = c_first + i;
+          uint4 cva[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+          const bool has_b = i + 1 < nchunks;
+          if (has_b) {
+            load_addend(c + 1, cv_next);
+            tmem_ld_32x32b_x32_async(tbase + 32 * (i + 1), vb);
           }
-          process(c + 1, vb, cvb);
-          if (has_a) {
-            tmem_ld_wait_regs(va);
-            if (c + 2 == nchunks - 1) release();
+          process(c, va, cva);
+          if (has_b) {
+            tmem_ld_wait_regs(vb);
+            if (i + 1 == nchunks - 1) release();
+            uint4 cvb[4] = {cv_next[0], cv_next[1], cv_next[2], cv_next[3]};
+            const bool has_a = i + 2 < nchunks;
+            if (has_a) {
+              load_addend(c + 2, cv_next);
+              tmem_ld_32x32b_x32_async(tbase + 32 * (i + 2), va);
+            }
+            process(c + 1, vb, cvb);
+            if (has_a) {
+              tmem_ld_wait_regs(va);
+              if (i + 2 == nchunks - 1) release();
+            }
           }
         }
       }

@@ -13,6 +13,15 @@
 // a CTA stores a block it computed only if it lies on or above the diagonal,
 // mirrored when strictly above (so each block pair still has one owner).
 //
+// Triangle storage (used inside a circuit): a symmetric result may be stored
+// as its blocks on and above the diagonal only (store_mirror = 0), and an
+// operand stored that way (a_tri / b_tri) is read back as a full matrix: a
+// k-block whose 128x128 block lies below the diagonal is loaded from the
+// stored transposed block with the other operand majorness (TMA box and UMMA
+// descriptor switch per k-block). One instruction serves both CTAs' halves,
+// so the pair switches together; it may then read a diagonal block
+// transposed, which is exact because those blocks are bit-symmetric.
+//
 // Pipeline, per pair: both producers wait for their own free stage and load
 // into their own shared memory, counting bytes on the leader's full barrier
 // (the leader alone arms it with both CTAs' bytes); the leader's UMMA thread
@@ -56,12 +65,12 @@ struct PairArgs {
   const __half* C;
   long long c_ld, c_bs;
   int has_addend, has_diag;
+  int a_tri, b_tri;       // operand stored as upper-triangle blocks only
+  int store_mirror;       // symmetric: also store the transposed off-diagonal blocks
   int* status;
   long long wait_limit;
 };
 
-// Tile t of the pair -> batch b, this CTA's first row m0, the tile's first
-// column n0 (256 columns; this CTA stages B columns n0 + 128 * rank ...).
 template <bool SYM>
 __device__ __forceinline__ void decode(const PairArgs& a, int t, uint32_t rank, int& b, int& m0,
                                        int& n0) {
@@ -90,8 +99,12 @@ __device__ __forceinline__ void decode(const PairArgs& a, int t, uint32_t rank, 
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     ps_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmA2,
                         const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmB2,
                         const __grid_constant__ CUtensorMap tmD, const PairArgs args) {
+  // tmA / tmB: boxes in the operand's native majorness (A_MN / B_MN);
+  // tmA2 / tmB2: the other majorness, used only for triangle-stored operands.
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -130,6 +143,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmD);
+    if (args.a_tri) tma_prefetch_desc(&tmA2);
+    if (args.b_tri) tma_prefetch_desc(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -154,6 +169,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int b, m0, n0;
         decode<SYM>(args, t, rank, b, m0, n0);
         const int nb = n0 + static_cast<int>(rank) * BNH;  // this CTA's half of B
+        const int a_lo = (m0 - static_cast<int>(rank) * BM) / BM;  // leader's row block
+        const int b_lo = n0 / BM;                                 // leader's B block
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status,
                                  kStatusProducerTimeout, args.wait_limit)) {
@@ -165,19 +182,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
           const int k0 = kb * BK;
-          if (!A_MN) {
-            tma_load_3d_pair(&tmA, a_dst, bar, k0, m0, b);
+          const bool at = args.a_tri && tri_transposed(A_MN, a_lo, a_lo + 1, k0 / BM);
+          const bool bt = args.b_tri && tri_transposed(B_MN, b_lo, b_lo + 1, k0 / BM);
+          const CUtensorMap* ma = at ? &tmA2 : &tmA;
+          const CUtensorMap* mb = bt ? &tmB2 : &tmB;
+          if (A_MN == at) {  // K-major tile
+            tma_load_3d_pair(ma, a_dst, bar, k0, m0, b);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
-              tma_load_3d_pair(&tmA, a_dst + j * MN_ATOM_BYTES, bar, m0 + 64 * j, k0, b);
+              tma_load_3d_pair(ma, a_dst + j * MN_ATOM_BYTES, bar, m0 + 64 * j, k0, b);
           }
-          if (!B_MN) {
-            tma_load_3d_pair(&tmB, b_dst, bar, k0, nb, b);
+          if (B_MN == bt) {
+            tma_load_3d_pair(mb, b_dst, bar, k0, nb, b);
           } else {
 #pragma unroll
             for (int j = 0; j < BNH / 64; ++j)
-              tma_load_3d_pair(&tmB, b_dst + j * MN_ATOM_BYTES, bar, nb + 64 * j, k0, b);
+              tma_load_3d_pair(mb, b_dst + j * MN_ATOM_BYTES, bar, nb + 64 * j, k0, b);
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -211,7 +232,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued_any = false;
-      const uint32_t idesc = make_idesc_f16(2 * BM, BN, A_MN, B_MN);
+
       const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), peer);
       const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), peer);
       for (int t = pair_id; t < args.total_tiles && ok; t += npairs) {
@@ -222,6 +243,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        int tb_, tm0_, tn0_;
+        decode<SYM>(args, t, 0, tb_, tm0_, tn0_);
+        const int a_lo = tm0_ / BM, b_lo = tn0_ / BM;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.status, kStatusMmaTimeout,
                                  args.wait_limit)) {
@@ -231,12 +255,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_STAGE_BYTES;
+          const int kb128 = (kb * BK) / BM;
+          const bool a_mn = A_MN != (args.a_tri && tri_transposed(A_MN, a_lo, a_lo + 1, kb128));
+          const bool b_mn = B_MN != (args.b_tri && tri_transposed(B_MN, b_lo, b_lo + 1, kb128));
+          const uint32_t idesc = make_idesc_f16(2 * BM, BN, a_mn, b_mn);
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint64_t ad = A_MN ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
+            const uint64_t ad = a_mn ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
                                                             MN_ATOM_BYTES, 1024)
                                      : make_smem_desc_sw128(a_addr + kk * (UMMA_K * 2), 16, 1024);
-            const uint64_t bd = B_MN ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
+            const uint64_t bd = b_mn ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
                                                             MN_ATOM_BYTES, 1024)
                                      : make_smem_desc_sw128(b_addr + kk * (UMMA_K * 2), 16, 1024);
             umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
@@ -276,7 +304,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     constexpr int BUF_BYTES = 32 * ROW_BYTES;
     constexpr int SLOT_BYTES = SYM ? 2 * BUF_BYTES : BUF_BYTES;
     constexpr int NSLOT = EPI_WARP_BYTES / SLOT_BYTES;
-    static_assert(NSLOT >= 2, "epilogue staging needs at least two slots");
+    static_assert(NSLOT >= 1, "epilogue staging needs a slot");
     static_assert(!SYM || OUT == kOutF16, "symmetric products are stored in FP16");
     const int q = warp & 3;               // TMEM lane quarter
     const int h = (warp - 2) >> 2;        // column half of the 256-column accumulator
@@ -345,7 +373,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         uint32_t w[32];
         convert_row<OUT>(f, w);
-        const bool mirror = SYM && (gcol0 / BM) != (m0 / BM);
+        const bool mirror = SYM && args.store_mirror && (gcol0 / BM) != (m0 / BM);
         if (lane == 0) bulk_wait_read<NSLOT - 1>();
         __syncwarp();
         const uint32_t sb = stg + slot * SLOT_BYTES;

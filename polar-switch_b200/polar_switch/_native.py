@@ -171,5 +171,5 @@ def profile_read():
 
 
 def set_cta_pairs(enable):
-    """Select the CTA-pair GEMM kernel (True, default) or the one-CTA kernel; returns the previous."""
+    """Select the CTA-pair GEMM kernel (True) or the one-CTA kernel (False, default); returns the previous."""
     return bool(load().ps_set_cta_pairs(1 if enable else 0))

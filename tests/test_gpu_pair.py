@@ -97,3 +97,19 @@ def test_circuit_pair_vs_single(cuda_device):
     polar = make_polynomial_orthogonalizer("PS3_55")
     pair, single = _both(lambda: polar(X))
     assert oc.relative_frobenius(pair, single) < 2e-3
+
+
+@pytest.mark.parametrize("method,shape", [("PS2_55", (2, 384, 1152)), ("PS3_55", (1152, 640)),
+                                          ("POLAR_EXPRESS", (3, 256, 384)), ("PS2_55", (1, 200, 72))])
+def test_triangle_storage_circuit_is_bit_identical(cuda_device, method, shape):
+    """Inside a circuit the square buffers are kept as upper-triangle blocks and
+    read back transposed; the result must equal, bit for bit, the op-by-op
+    evaluation through the public kernels that store full mirrored buffers."""
+    import polar_switch
+    from polar_switch import coefficients, cuda_ops
+    X = seeded(shape, 350).to(cuda_device)
+    table = getattr(coefficients, method)
+    fused = polar_switch.make_polynomial_orthogonalizer(method)(X)
+    buffers = polar_switch.validate_table(table, 1e-7)
+    op_by_op = polar_switch._run(X, table, cuda_ops, 1e-7, buffers).to(X.dtype)
+    assert torch.equal(fused, op_by_op)
