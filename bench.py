@@ -202,7 +202,7 @@ def config_dict(args, shapes, method):
     return {"workload": f"{args.workload}: {WORKLOADS[args.workload]['desc']}", "method": method,
             "matrices": total, "banks": [list(s) for s in shapes], "input": "fp32 N(0,1), seed 0",
             "l2": f"inputs larger than L2 ({in_bytes / 1e9:.2f} GB per step vs 126 MB L2)",
-            "parallelism": f"matrix-sharded x{args.gpus}, NCCL all-gather of FP16 updates"}
+            "parallelism": f"matrix-sharded x{args.gpus}, FP16 updates gathered over NVLink"}
 
 
 def run_kernel(args):
@@ -274,6 +274,13 @@ def main():
                     help="time one kernel class alone (for profiling) instead of the whole step")
     ap.add_argument("--bank", type=int, default=0, help="bank of the workload used by --kernel")
     ap.add_argument("--L", type=int, default=0, help="--kernel: override the number of matrices")
+    ap.add_argument("--buckets", default=None,
+                    help="multi-GPU: bucket count, or comma-separated cost fractions, of the "
+                         "gather/compute overlap (default: auto)")
+    ap.add_argument("--gemm-ctas", type=int, default=None,
+                    help="multi-GPU: cap on GEMM CTAs, leaving SMs to the all-gather")
+    ap.add_argument("--transport", default="auto", choices=["auto", "copy_engine", "collective"],
+                    help="multi-GPU: copy-engine pushes into symmetric memory, or the NCCL all-gather")
     args = ap.parse_args()
     if args.kernel:
         run_kernel(args)
@@ -294,8 +301,12 @@ def main():
     shapes = bank_shapes(args.workload)
     method = WORKLOADS[args.workload]["method"]
     banks = make_banks(shapes, device, seed=0)
+    buckets = args.buckets
+    if buckets is not None:
+        buckets = [float(f) for f in buckets.split(",")] if "," in buckets else int(buckets)
     step = ShardedOrthogonalizer(shapes, method=method, group=None, device=device,
-                                 world_size=world, rank=rank)
+                                 world_size=world, rank=rank, buckets=buckets,
+                                 gemm_ctas=args.gemm_ctas, transport=args.transport)
     flops = step.flops_total
 
     def barrier():
@@ -337,15 +348,13 @@ def main():
     # gathered FP16 update set.
     host_banks = [b.cpu().pin_memory() for b in banks]
     host_out = torch.empty(step.recv.numel(), dtype=torch.float16).pin_memory()
-    h2d = 0
-    for rank_slice, (L, r, c) in zip(step.slices[rank], shapes):
-        h2d += rank_slice[1] * r * c * 4
+    ranges = step.local_ranges()
+    h2d = sum(count * shapes[g][1] * shapes[g][2] * 4 for g, _, count in ranges)
     dev_banks = [torch.empty_like(b) for b in banks]
 
     def e2e_step():
-        for hb, db, (start, count) in zip(host_banks, dev_banks, step.slices[rank]):
-            if count:
-                db[start:start + count].copy_(hb[start:start + count], non_blocking=True)
+        for g, start, count in ranges:
+            dev_banks[g][start:start + count].copy_(host_banks[g][start:start + count], non_blocking=True)
         out = step(dev_banks)
         host_out.copy_(out, non_blocking=True)
 
@@ -407,10 +416,17 @@ def main():
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
         }
+        if world > 1:
+            line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
+                                        "gemm_ctas": args.gemm_ctas,
+                                        "bucket_matrices": [sum(c for _, _, c in p["pieces"]) for p in step.plans],
+                                        "bytes_per_step": step.recv.numel() * 2}
         if args.workload == "single":
             line["vs_baseline"] = value / 1177.0  # published 7.47 ms for 8192^2 PS2-55
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize(device)
+        step.close()
         dist.barrier()
         dist.destroy_process_group()
 

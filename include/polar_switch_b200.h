@@ -95,6 +95,11 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
  * Returns the previous setting. */
 PS_API int ps_set_cta_pairs(int enable);
 
+/* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
+ * afterwards; 0 (default) = every SM. Leaving SMs free lets a collective on
+ * another stream run beside the GEMMs. Returns the previous cap. */
+PS_API int ps_set_max_ctas(int max_ctas);
+
 /* Launches one kernel whose single wait can never be satisfied, so that it
  * runs out after `limit_cycles` and records its status code (5). Used by the
  * tests of the bounded-wait path. */

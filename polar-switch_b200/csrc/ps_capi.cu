@@ -51,6 +51,9 @@ long long g_wait_limit = ps::kDefaultWaitLimit;
 // GEMMs run on the one-CTA kernel unless CTA pairs (cta_group::2) are selected
 // with ps_set_cta_pairs; measured faster on every circuit shape.
 bool g_use_pair = false;
+// Upper bound on the CTAs (SMs) a persistent GEMM grid may take; 0 = all SMs.
+// Leaving SMs free lets a collective run beside the GEMMs.
+int g_max_ctas = 0;
 
 // Every kernel launch of the library is counted; when profiling is enabled,
 // each launch is also bracketed by CUDA events on its stream and tagged with
@@ -304,8 +307,9 @@ int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& ta2,
   if (args.total_tiles <= 0) return PS_OK;
   args.status = st->status;
   args.wait_limit = g_wait_limit;
-  const int pairs = args.total_tiles < st->pair_clusters[variant] ? args.total_tiles
-                                                                  : st->pair_clusters[variant];
+  int pairs = args.total_tiles < st->pair_clusters[variant] ? args.total_tiles
+                                                            : st->pair_clusters[variant];
+  if (g_max_ctas > 1 && pairs > g_max_ctas / 2) pairs = g_max_ctas / 2;
   cfg.gridDim = dim3(2 * pairs);
   LaunchScope scope(kind, stream, flops, bytes);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, ta2, tb, tb2, td, args);
@@ -339,7 +343,8 @@ int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const
   if (args.total_tiles <= 0) return PS_OK;
   args.status = st->status;
   args.wait_limit = g_wait_limit;
-  const int grid = args.total_tiles < st->sms ? args.total_tiles : st->sms;
+  int grid = args.total_tiles < st->sms ? args.total_tiles : st->sms;
+  if (g_max_ctas > 0 && grid > g_max_ctas) grid = g_max_ctas;
   LaunchScope scope(kind, stream, flops, bytes);
   kern<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(ta, ta2 ? *ta2 : ta, tb,
                                                            tb2 ? *tb2 : tb, td, args);
@@ -812,6 +817,13 @@ int ps_profile_read(int kind, double* total_ms, int64_t* launches, double* flops
   *flops = f;
   *bytes = b;
   return PS_OK;
+}
+
+int ps_set_max_ctas(int max_ctas) {
+  if (max_ctas < 0) return fail(PS_ERR_INVALID, "ps_set_max_ctas: negative limit");
+  const int previous = g_max_ctas;
+  g_max_ctas = max_ctas;
+  return previous;
 }
 
 int ps_set_cta_pairs(int enable) {

@@ -29,6 +29,7 @@ EXPORTED = (
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
     "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs",
+    "ps_set_max_ctas",
 )
 
 
@@ -83,6 +84,7 @@ _SIGNATURES = {
                     _int, _f32, _ptr, _i64, _ptr], _int),
     "ps_launch_count": ([], ctypes.c_longlong),
     "ps_set_cta_pairs": ([_int], _int),
+    "ps_set_max_ctas": ([_int], _int),
     "ps_profile_enable": ([_int], _int),
     "ps_profile_read": ([_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64),
                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], _int),
@@ -173,3 +175,11 @@ def profile_read():
 def set_cta_pairs(enable):
     """Select the CTA-pair GEMM kernel (True) or the one-CTA kernel (False, default); returns the previous."""
     return bool(load().ps_set_cta_pairs(1 if enable else 0))
+
+
+def set_max_ctas(max_ctas):
+    """Cap the CTAs of persistent GEMM grids (0 = all SMs); returns the previous cap."""
+    rc = load().ps_set_max_ctas(int(max_ctas))
+    if rc < 0:
+        check("ps_set_max_ctas", rc)
+    return rc

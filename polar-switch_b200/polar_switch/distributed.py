@@ -10,10 +10,14 @@ training/train_nanogpt.py:3983-4037, 4119-4218). Here
     on the per-matrix circuit FLOPs so every rank gets about the same work;
     the plan is a pure function of the shapes, so every rank computes the same
     plan without communication;
-  * `ShardedOrthogonalizer` runs the local slices as one grouped circuit whose
-    FP16 results land directly in a packed send buffer (the circuit rounds to
-    FP16, so FP16 is lossless), then one NCCL all_gather_into_tensor gives
-    every rank all updates. With one rank nothing is communicated.
+  * `plan_buckets` cuts the matrices into a few consecutive buckets of about
+    equal cost, so communication of one bucket overlaps the next one's math;
+  * `ShardedOrthogonalizer` runs each bucket's local slices as one grouped
+    circuit whose FP16 results land directly in that bucket's packed send
+    segment (the circuit rounds to FP16, so FP16 is lossless), then an
+    asynchronous in-place NCCL all_gather_into_tensor of the bucket gives every
+    rank its updates while the next bucket computes. With one rank nothing is
+    communicated.
 """
 
 import heapq
@@ -64,21 +68,117 @@ def plan_loads(banks, slices, flops_fn):
             for rank in slices]
 
 
+def plan_buckets(banks, buckets, flops_fn):
+    """Split the matrices of all banks into consecutive buckets by cost.
+
+    Args:
+        banks: list of (L, rows, cols).
+        buckets: number of buckets of about equal cost, or a list of cost
+            fractions (normalised to sum 1), first bucket first.
+        flops_fn: flops_fn(rows, cols) -> cost of one matrix.
+
+    Returns:
+        list of buckets, each a list of (bank, start, count) pieces covering
+        consecutive matrices of a bank; every matrix is in exactly one piece.
+        Empty buckets are dropped.
+    """
+    fracs = [1.0] * buckets if isinstance(buckets, int) else [float(f) for f in buckets]
+    if not fracs or any(f <= 0 for f in fracs):
+        raise ValueError("buckets must be a positive count or a list of positive fractions")
+    total = sum(L * flops_fn(r, c) for L, r, c in banks)
+    bounds, acc = [], 0.0
+    for f in fracs:
+        acc += f
+        bounds.append(total * acc / sum(fracs))
+    out = [[] for _ in fracs]
+    k, done = 0, 0.0
+    for g, (L, rows, cols) in enumerate(banks):
+        cost = flops_fn(rows, cols)
+        i = 0
+        while i < L:
+            # Matrices of this bank that still fit the current bucket (at least one).
+            room = bounds[k] - done
+            take = L - i if k == len(fracs) - 1 else max(1, min(L - i, int(room / cost + 0.5)))
+            out[k].append((g, i, take))
+            i += take
+            done += take * cost
+            if k < len(fracs) - 1 and done >= bounds[k] - 0.5 * cost:
+                k += 1
+    return [b for b in out if b]
+
+
+# Rates used only to shape the buckets: the whole-step circuit rate of one
+# B200 on n ~ 1024 matrices, the rate at which a GPU receives the gathered
+# updates over NVLink (copy-engine pushes: ~0.7 TB/s at 2 and 8 GPUs), and the
+# fixed cost of running a bucket as its own circuit (launch tails of its
+# ~40 kernels), all measured on B200.
+CIRCUIT_FLOPS_PER_S = 7.5e14
+GATHER_RECV_BYTES_PER_S = 7.0e11
+BUCKET_OVERHEAD_S = 2.0e-4
+
+
+def simulate_buckets(fractions, compute_s, gather_s, overhead_s=BUCKET_OVERHEAD_S):
+    """Modelled step time of a bucket schedule: the circuits run back to back on
+    one stream, each bucket's gather starts when its circuits and the previous
+    gather are done."""
+    total = float(sum(fractions))
+    t_compute = t_gather = 0.0
+    for f in fractions:
+        t_compute += overhead_s + compute_s * f / total
+        t_gather = max(t_gather, t_compute) + gather_s * f / total
+    return t_gather
+
+
+def auto_bucket_fractions(banks, world_size, flops_fn):
+    """Bucket cost fractions for overlapping the gather with the circuits.
+
+    Candidates are geometric schedules (fractions proportional to r**k, k <
+    count): r < 1 front-loads the work, so a compute-bound step exposes only a
+    small last gather; r > 1 starts a gather-bound step's transfers early. The
+    candidate with the least modelled step time (`simulate_buckets`) wins.
+    """
+    flops = sum(L * flops_fn(r, c) for L, r, c in banks)
+    elems = sum(L * r * c for L, r, c in banks)
+    if world_size < 2 or flops <= 0:
+        return 1
+    compute_s = flops / world_size / CIRCUIT_FLOPS_PER_S
+    gather_s = (world_size - 1) / world_size * elems * 2 / GATHER_RECV_BYTES_PER_S
+    best = ([1.0], simulate_buckets([1.0], compute_s, gather_s))
+    for count in (2, 3, 4, 5):
+        for r in (0.2, 0.25, 1 / 3, 0.5, 0.7, 1.0, 1.4, 2.0, 3.0):
+            fr = [r ** k for k in range(count)]
+            t = simulate_buckets(fr, compute_s, gather_s)
+            if t < best[1] * (1 - 1e-9):
+                best = (fr, t)
+    return best[0]
+
+
 class ShardedOrthogonalizer:
     """Orthogonalize banks of matrices across the ranks of a process group.
 
     Every rank passes the same list of banks (CUDA tensors (L_g, rows_g,
-    cols_g), e.g. momentum buffers after gradient averaging); each rank
-    orthogonalizes its slice of every bank and the FP16 results are
-    all-gathered. ``__call__`` returns the gathered buffer; ``bank_updates``
-    gives, per bank, the (start, view) slices of the result.
+    cols_g), e.g. momentum buffers after gradient averaging). The matrices are
+    cut into buckets of consecutive matrices (`plan_buckets`); each bucket is
+    split across the ranks by `plan_shards`, orthogonalized as one grouped
+    circuit, and its FP16 results are all-gathered asynchronously while the
+    next bucket computes. ``__call__`` returns the gathered buffer (stream-
+    ordered); ``bank_updates`` gives, per bank, the (start, view) slices of it.
     """
 
     def __init__(self, bank_shapes, method="PS2_55", epsilon=1e-7, group=None, device=None,
-                 world_size=None, rank=None, grouped_fn=None):
+                 world_size=None, rank=None, grouped_fn=None, buckets=None, gemm_ctas=None,
+                 transport="auto"):
         """``grouped_fn(inputs, outs)`` replaces the B200 grouped circuit (used by
         the CPU tests of the sharding logic); by default the circuit runs on
-        the GPU."""
+        the GPU. ``buckets``: number of buckets or their cost fractions; by
+        default 1 on one rank and `auto_bucket_fractions` otherwise. ``gemm_ctas``: cap on the CTAs of the GEMM
+        grids while a gather may be in flight, leaving SMs to the collective
+        (None = no cap). ``transport``: how a bucket reaches the other ranks:
+        "copy_engine" (each rank pushes its segment into every peer's receive
+        buffer, a symmetric-memory allocation, with peer-to-peer copies that
+        run on the copy engines and leave every SM to the circuits),
+        "collective" (an asynchronous all_gather_into_tensor of the group's
+        backend) or "auto" (copy engines on CUDA, else the collective)."""
         self.group = group
         if world_size is None:
             world_size = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -86,66 +186,180 @@ class ShardedOrthogonalizer:
             rank = dist.get_rank(group) if world_size > 1 else 0
         self.world_size, self.rank = world_size, rank
         self.polar = make_polynomial_orthogonalizer(method, epsilon=epsilon)
+        self.native_circuit = grouped_fn is None
         self.grouped_fn = grouped_fn or (lambda inputs, outs: self.polar.grouped(inputs, outs=outs))
+        self.gemm_ctas = gemm_ctas
         table = self.polar.table
         self.flops_fn = lambda r, c: circuit_flops(table, r, c)
         self.bank_shapes = [tuple(int(v) for v in s) for s in bank_shapes]
-        self.slices = plan_shards(self.bank_shapes, world_size, self.flops_fn)
-        self.seg_elems = []
-        for rank_slices in self.slices:
-            self.seg_elems.append(sum(c * r * k for (_, c), (_, r, k) in zip(rank_slices, self.bank_shapes)))
-        # Pad every rank's segment to a multiple of 128 elements (256 B) so the
-        # per-problem outputs stay 16-byte aligned.
-        self.seg = max(-(-e // 128) * 128 for e in self.seg_elems) if self.seg_elems else 0
+        if buckets is None:
+            buckets = 1 if world_size == 1 else auto_bucket_fractions(self.bank_shapes, world_size,
+                                                                       self.flops_fn)
+        self.buckets = plan_buckets(self.bank_shapes, buckets, self.flops_fn)
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
-        # In-place all-gather: this rank's segment of the receive buffer is the
-        # send buffer, so the circuit writes its results where they end up.
-        self.recv = torch.empty(world_size * max(self.seg, 1), device=self.device, dtype=torch.float16)
-        self.send = self.recv[rank * self.seg:(rank + 1) * self.seg]
+        # Per bucket: the sub-banks it holds, their split across ranks and the
+        # padded per-rank segment length. Segments are padded to a multiple of
+        # 128 elements (256 B) so the per-problem outputs stay 16-byte aligned.
+        self.plans = []
+        offset = 0
+        for pieces in self.buckets:
+            shapes = [(count, self.bank_shapes[g][1], self.bank_shapes[g][2]) for g, _, count in pieces]
+            slices = plan_shards(shapes, world_size, self.flops_fn)
+            elems = [sum(c * r * k for (_, c), (_, r, k) in zip(rs, shapes)) for rs in slices]
+            seg = max(max(-(-e // 128) * 128 for e in elems), 128)
+            self.plans.append({"pieces": pieces, "slices": slices, "seg": seg, "offset": offset})
+            offset += world_size * seg
+        # In-place gathers: this rank's segment of each bucket's receive region
+        # is its send buffer, so the circuit writes results where they end up.
+        if transport not in ("auto", "copy_engine", "collective"):
+            raise ValueError(f"unknown transport {transport!r}")
+        if transport == "auto":
+            transport = "copy_engine" if world_size > 1 and self.device.type == "cuda" else "collective"
+        if world_size == 1:
+            transport = "none"
+        self.transport = transport
+        numel = max(offset, 1)
+        if transport == "copy_engine":
+            import torch.distributed._symmetric_memory as symm
+            self.recv = symm.empty(numel, device=self.device, dtype=torch.float16)
+            handle = symm.rendezvous(self.recv, self.group if self.group is not None else dist.group.WORLD)
+            self._peer_recv = [handle.get_buffer(p, (numel,), torch.float16) for p in range(world_size)]
+            self._handle = handle
+            self._comm = torch.cuda.Stream(device=self.device)
+            self._flag = torch.zeros(1, device=self.device, dtype=torch.int32)
+        else:
+            self.recv = torch.empty(numel, device=self.device, dtype=torch.float16)
         self.flops_total = sum(L * self.flops_fn(r, c) for L, r, c in self.bank_shapes)
-        self.flops_per_rank = plan_loads(self.bank_shapes, self.slices, self.flops_fn)
+        self.flops_per_rank = [0.0] * world_size
+        for plan in self.plans:
+            shapes = [(c, self.bank_shapes[g][1], self.bank_shapes[g][2]) for g, _, c in plan["pieces"]]
+            for r, load in enumerate(plan_loads(shapes, plan["slices"], self.flops_fn)):
+                self.flops_per_rank[r] += load
 
-    def _segment_views(self, buf, rank):
-        """Views of one rank's packed segment, one per non-empty bank slice."""
+    def _region(self, plan):
+        return self.recv[plan["offset"]:plan["offset"] + self.world_size * plan["seg"]]
+
+    def _segment(self, plan, rank):
+        base = plan["offset"] + rank * plan["seg"]
+        return self.recv[base:base + plan["seg"]]
+
+    def _segment_views(self, plan, rank):
+        """(bank, start within the bank, view) for each non-empty slice of one
+        rank's segment of a bucket."""
         views, off = [], 0
-        for g, ((start, count), (_, rows, cols)) in enumerate(zip(self.slices[rank], self.bank_shapes)):
+        seg = self._segment(plan, rank)
+        for (g, base, _), (start, count) in zip(plan["pieces"], plan["slices"][rank]):
             if count:
+                rows, cols = self.bank_shapes[g][1:]
                 n = count * rows * cols
-                views.append((g, start, buf[off:off + n].view(count, rows, cols)))
+                views.append((g, base + start, seg[off:off + n].view(count, rows, cols)))
                 off += n
         return views
 
-    def compute_local(self, banks):
-        """Orthogonalize this rank's slices into the packed send buffer (no communication)."""
+    def local_ranges(self, rank=None):
+        """(bank, start, count) of every matrix range the given rank orthogonalizes."""
+        rank = self.rank if rank is None else rank
+        return [(g, start, v.shape[0]) for plan in self.plans for g, start, v in self._segment_views(plan, rank)]
+
+    def _check(self, banks):
         if len(banks) != len(self.bank_shapes):
             raise ValueError("expected one tensor per bank")
         for X, shape in zip(banks, self.bank_shapes):
             if tuple(X.shape) != shape:
                 raise ValueError(f"bank shape {tuple(X.shape)} does not match the plan {shape}")
+
+    def _compute_bucket(self, banks, plan):
         inputs, outputs = [], []
-        for g, start, view in self._segment_views(self.send, self.rank):
+        for g, start, view in self._segment_views(plan, self.rank):
             inputs.append(banks[g][start:start + view.shape[0]])
             outputs.append(view)
         if inputs:
             self.grouped_fn(inputs, outputs)
-        return self.send
+
+    def compute_local(self, banks):
+        """Orthogonalize this rank's slices into its segments (no communication)."""
+        self._check(banks)
+        for plan in self.plans:
+            self._compute_bucket(banks, plan)
+        return self.recv
 
     def __call__(self, banks):
-        """Orthogonalize all banks across the group; returns the gathered FP16 buffer."""
-        self.compute_local(banks)
-        if self.world_size > 1:
-            dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        """Orthogonalize all banks across the group; returns the gathered FP16
+        buffer (ready in the order of the current stream)."""
+        self._check(banks)
+        if self.world_size == 1:
+            return self.compute_local(banks)
+        cap = self.native_circuit and self.gemm_ctas
+        if cap:
+            from . import _native
+            previous = _native.set_max_ctas(self.gemm_ctas)
+        try:
+            if self.transport == "copy_engine":
+                self._step_copy_engine(banks)
+            else:
+                self._step_collective(banks)
+        finally:
+            if cap:
+                _native.set_max_ctas(previous)
         return self.recv
+
+    def _step_collective(self, banks):
+        works = []
+        try:
+            for plan in self.plans:
+                self._compute_bucket(banks, plan)
+                works.append(dist.all_gather_into_tensor(self._region(plan), self._segment(plan, self.rank),
+                                                         group=self.group, async_op=True))
+        finally:
+            for w in works:
+                w.wait()
+
+    def _barrier_on(self, stream):
+        """A group-wide barrier ordered on `stream` (a one-element all-reduce)."""
+        with torch.cuda.stream(stream):
+            dist.all_reduce(self._flag, group=self.group)
+
+    def _step_copy_engine(self, banks):
+        """Push each finished bucket into every peer's receive buffer from a side
+        stream while the next bucket computes on the current stream.
+
+        Ordering: the side stream first waits for the current stream and passes
+        a barrier, so no peer still reads the previous step's results when the
+        first push lands; after the last push a second barrier tells every rank
+        that all pushes into its buffer are complete, and the current stream
+        waits for it."""
+        main = torch.cuda.current_stream(self.device)
+        comm = self._comm
+        comm.wait_stream(main)
+        self._barrier_on(comm)
+        order = [(self.rank + i) % self.world_size for i in range(1, self.world_size)]
+        for plan in self.plans:
+            self._compute_bucket(banks, plan)
+            comm.wait_stream(main)
+            base = plan["offset"] + self.rank * plan["seg"]
+            src = self.recv[base:base + plan["seg"]]
+            with torch.cuda.stream(comm):
+                for p in order:
+                    self._peer_recv[p][base:base + plan["seg"]].copy_(src, non_blocking=True)
+        self._barrier_on(comm)
+        main.wait_stream(comm)
+
+    def close(self):
+        """Drop the peer mappings of the receive buffer (before the process
+        group is destroyed)."""
+        for name in ("_peer_recv", "_handle"):
+            if hasattr(self, name):
+                delattr(self, name)
 
     def bank_updates(self):
         """Per bank, the list of (start, FP16 view) slices of the gathered result."""
         out = [[] for _ in self.bank_shapes]
-        for r in range(self.world_size):
-            seg = self.recv[r * self.seg:(r + 1) * self.seg]
-            for g, start, view in self._segment_views(seg, r):
-                out[g].append((start, view))
+        for plan in self.plans:
+            for r in range(self.world_size):
+                for g, start, view in self._segment_views(plan, r):
+                    out[g].append((start, view))
         return out
 
     def gathered_banks(self):

@@ -61,7 +61,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shapes, result_queue, fail_rank):
+def _worker(rank, world, port, shapes, result_queue, fail_rank, buckets=None):
     try:
         import datetime
         import torch.distributed as dist
@@ -71,7 +71,7 @@ def _worker(rank, world, port, shapes, result_queue, fail_rank):
         g = torch.Generator().manual_seed(7)
         banks = [torch.randn(*s, generator=g) for s in shapes]  # same on every rank
         step = ShardedOrthogonalizer(shapes, method="PS2_55", device="cpu", world_size=world, rank=rank,
-                                     grouped_fn=_oracle_grouped)
+                                     grouped_fn=_oracle_grouped, buckets=buckets)
         if rank == fail_rank:
             raise RuntimeError("injected failure on the host before the collective")
         step(banks)
@@ -83,11 +83,11 @@ def _worker(rank, world, port, shapes, result_queue, fail_rank):
         result_queue.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
 
 
-def _run(world, shapes, fail_rank=-1, timeout=120):
+def _run(world, shapes, fail_rank=-1, timeout=120, buckets=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shapes, q, fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shapes, q, fail_rank, buckets)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -103,10 +103,10 @@ def _run(world, shapes, fail_rank=-1, timeout=120):
     return results
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_sharded_step_gloo_matches_single_process(world):
+@pytest.mark.parametrize("world,buckets", [(2, None), (4, None), (2, 1), (3, 3)])
+def test_sharded_step_gloo_matches_single_process(world, buckets):
     shapes = [(5, 48, 32), (3, 32, 32), (2, 32, 80)]
-    results = _run(world, shapes)
+    results = _run(world, shapes, buckets=buckets)
     assert sorted(results) == list(range(world))
     g = torch.Generator().manual_seed(7)
     banks = [torch.randn(*s, generator=g) for s in shapes]
@@ -125,3 +125,52 @@ def test_rank_failure_before_collective_is_reported():
     results = _run(2, shapes, fail_rank=1, timeout=180)
     assert isinstance(results[1], str) and "injected failure" in results[1]
     assert isinstance(results[0], str)  # the surviving rank saw the collective fail
+
+
+@pytest.mark.parametrize("banks", [qwen3_0_6b_banks(), gemma3_1b_banks(), nanogpt_banks(), [(4, 8192, 28672)],
+                                   [(3, 64, 64), (1, 128, 32)], [(1, 256, 256)]])
+@pytest.mark.parametrize("buckets", [1, 2, 4, 7, [1, 3, 3, 1]])
+def test_buckets_cover_every_matrix_once(banks, buckets):
+    from polar_switch.distributed import plan_buckets
+    plan = plan_buckets(banks, buckets, flops)
+    nb = buckets if isinstance(buckets, int) else len(buckets)
+    assert 1 <= len(plan) <= nb
+    seen = [[] for _ in banks]
+    for pieces in plan:
+        assert pieces
+        for g, start, count in pieces:
+            assert count > 0
+            seen[g].extend(range(start, start + count))
+    assert seen == [list(range(L)) for L, _, _ in banks]
+    if isinstance(buckets, int) and sum(L for L, _, _ in banks) >= 8 * buckets:
+        costs = [sum(c * flops(*banks[g][1:]) for g, _, c in p) for p in plan]
+        biggest = max(flops(r, c) for _, r, c in banks)
+        assert max(costs) <= sum(costs) / buckets + biggest + 1e-6
+
+
+@pytest.mark.parametrize("buckets", [1, 3])
+def test_bucketed_layout_single_rank_views(buckets):
+    """Offsets of the bucketed receive buffer: every rank's views are disjoint,
+    16-byte aligned, and together cover each bank once."""
+    shapes = qwen3_0_6b_banks()
+    world = 4
+    views = []
+    for r in range(world):
+        step = ShardedOrthogonalizer(shapes, method="PS2_55", device="meta", world_size=world, rank=r,
+                                     grouped_fn=_oracle_grouped, buckets=buckets)
+        for plan in step.plans:
+            for g, start, v in step._segment_views(plan, r):
+                off = v.storage_offset()
+                assert off % 8 == 0
+                views.append((off, off + v.numel(), g, start, v.shape[0]))
+        assert sum(c for _, _, c in step.local_ranges()) == sum(
+            c for plan in step.plans for _, c in plan["slices"][r])
+    views.sort()
+    for a, b in zip(views, views[1:]):
+        assert a[1] <= b[0]
+    for g, (L, _, _) in enumerate(shapes):
+        got = sorted((s, c) for _, _, gg, s, c in views if gg == g)
+        cover = []
+        for s, c in got:
+            cover.extend(range(s, s + c))
+        assert cover == list(range(L))

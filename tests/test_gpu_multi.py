@@ -1,0 +1,82 @@
+"""The sharded Muon step on 2 GPUs (one process per GPU, NCCL): both gather
+transports (copy-engine pushes into symmetric memory, and the NCCL
+all-gather) must give every rank exactly the updates a single process
+computes for the same banks. Skipped with fewer than two GPUs."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(6, 256, 128), (5, 128, 128), (3, 128, 384), (2, 136, 200)]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, transport, buckets, q):
+    try:
+        import datetime
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [os.path.join(root, "polar-switch_b200"), root]
+        import torch.distributed as dist
+        from polar_switch import make_polynomial_orthogonalizer
+        from polar_switch.distributed import ShardedOrthogonalizer
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        g = torch.Generator().manual_seed(11)
+        banks = [torch.randn(*s, generator=g).to(dev) for s in SHAPES]
+        step = ShardedOrthogonalizer(SHAPES, method="PS2_55", device=dev, transport=transport,
+                                     buckets=buckets)
+        for _ in range(2):  # a second step reuses the buffers behind the barriers
+            step(banks)
+        got = [t.cpu() for t in step.gathered_banks()]
+        polar = make_polynomial_orthogonalizer("PS2_55")
+        want = [polar(b).half().cpu() for b in banks]
+        torch.cuda.synchronize()
+        step.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, step.transport, [torch.equal(a, b) for a, b in zip(got, want)]))
+    except Exception as e:
+        q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+@pytest.mark.parametrize("transport,buckets", [("copy_engine", None), ("copy_engine", 3),
+                                               ("collective", 2)])
+def test_two_gpu_step_matches_single_process(cuda_device, transport, buckets):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, buckets, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, used, res = q.get(timeout=240)
+            results[rank] = (used, res)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank in range(2):
+        used, res = results[rank]
+        assert not isinstance(res, str), res
+        assert used == transport
+        assert all(res), res
