@@ -21,10 +21,21 @@ intervals (reference README.md:64-73).
 import torch
 
 
+def frobenius_norm_f32(X):
+    """||X||_F of FP32 matrices, rounded once to FP32 from an FP64 sum.
+
+    The reference takes torch's FP32 norm of a CUDA tensor (a tree reduction,
+    within an ulp or two of the exact value). Torch's FP32 norm on the CPU
+    drifts far more on large matrices (about 6e-5 relative at 3M elements),
+    so the oracle rounds the exact norm instead.
+    """
+    return X.double().pow(2).sum(dim=(-2, -1), keepdim=True).sqrt().float()
+
+
 def normalize(X, epsilon):
     """fp16(fp32(X) / (||fp32(X)||_F + eps)) per matrix (reference __init__.py:34-35)."""
     X = X.float()
-    return (X / (X.norm(dim=(-2, -1), keepdim=True) + epsilon)).half().contiguous()
+    return (X / (frobenius_norm_f32(X) + epsilon)).half().contiguous()
 
 
 TILE = 128

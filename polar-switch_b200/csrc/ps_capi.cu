@@ -555,18 +555,34 @@ int norm_chunks(int64_t L, int64_t rows, int64_t cols, int sms) {
 
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
+// Canonical chunk count of a contiguous matrix of E elements (ps_norm.cuh).
+int64_t norm_flat_chunks(int64_t E) {
+  const int64_t ce = ps::norm_chunk_elems(E);
+  return (E + ce - 1) / ce;
+}
+
+// Partial sums one matrix may need: canonical chunks (contiguous input) or
+// row ranges (strided input).
+int64_t norm_partials_per_matrix(int64_t L, int64_t rows, int64_t cols, int sms) {
+  const int64_t a = norm_flat_chunks(rows * cols), b = norm_chunks(L, rows, cols, sms);
+  return a > b ? a : b;
+}
+
+// Two passes. Contiguous input is summed over chunks of `chunk_elems`
+// elements, strided input over `chunks` row ranges.
 template <typename T>
 int launch_normalize(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL, int64_t sR,
                      int64_t sC, float eps, void* xh, int64_t Rp, int64_t Cp, double* partial,
-                     int chunks, int sms, cudaStream_t s) {
+                     int chunks, int64_t chunk_elems, int sms, cudaStream_t s) {
   const int flat = (sC == 1 && sR == C) ? 1 : 0;
+  if (flat) chunks = static_cast<int>((R * C + chunk_elems - 1) / chunk_elems);
   dim3 g1(chunks, static_cast<unsigned>(L));
   const double in_bytes = static_cast<double>(L) * R * C * sizeof(T);
   cudaError_t e;
   {
     LaunchScope scope(kProfNormalize, s, 2.0 * L * R * C, in_bytes);
     ps::ps_norm_partial_kernel<T><<<g1, ps::NORM_THREADS, 0, s>>>(
-        static_cast<const T*>(x), R, C, sL, sR, sC, flat, chunks, partial);
+        static_cast<const T*>(x), R, C, sL, sR, sC, flat, chunks, chunk_elems, partial);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 1)");
@@ -588,7 +604,9 @@ int launch_normalize(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL,
 }
 
 int64_t normalize_ws_bytes(int64_t L, int64_t rows, int64_t cols, int sms) {
-  return round_up(L * norm_chunks(L, rows, cols, sms) * static_cast<int64_t>(sizeof(double)), 256);
+  return round_up(L * norm_partials_per_matrix(L, rows, cols, sms) *
+                      static_cast<int64_t>(sizeof(double)),
+                  256);
 }
 
 int normalize_impl(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
@@ -606,19 +624,20 @@ int normalize_impl(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t 
   if (ws_bytes < normalize_ws_bytes(L, rows, cols, st->sms))
     return fail(PS_ERR_WORKSPACE, "ps_normalize: workspace too small");
   double* partial = static_cast<double*>(ws);
+  const int64_t ce = ps::norm_chunk_elems(rows * cols);
   switch (x_dtype) {
     case PS_F16:
       return launch_normalize<__half>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp, partial,
-                                      chunks, st->sms, stream);
+                                      chunks, ce, st->sms, stream);
     case PS_BF16:
       return launch_normalize<__nv_bfloat16>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp,
-                                             partial, chunks, st->sms, stream);
+                                             partial, chunks, ce, st->sms, stream);
     case PS_F32:
       return launch_normalize<float>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp, partial,
-                                     chunks, st->sms, stream);
+                                     chunks, ce, st->sms, stream);
     default:
       return launch_normalize<double>(x, L, rows, cols, sL, sR, sC, eps, xh, Rp, Cp, partial,
-                                      chunks, st->sms, stream);
+                                      chunks, ce, st->sms, stream);
   }
 }
 
@@ -1074,22 +1093,26 @@ int ps_normalize_noalloc(const void* x, int x_dtype, int64_t L, int64_t rows, in
   int chunks = norm_chunks(L, rows, cols, st->sms);
   if (L * chunks > PS_NORMALIZE_NOALLOC_MAX_PARTIALS)
     chunks = static_cast<int>(PS_NORMALIZE_NOALLOC_MAX_PARTIALS / L);
+  int64_t ce = ps::norm_chunk_elems(rows * cols);
+  const int64_t max_per = PS_NORMALIZE_NOALLOC_MAX_PARTIALS / L;
+  if ((rows * cols + ce - 1) / ce > max_per)
+    ce = round_up((rows * cols + max_per - 1) / max_per, ps::NORM_CHUNK);
   // Pass 1 writes every one of the L * chunks partial sums before pass 2 reads
   // them, so nothing left in the scratch by an earlier call is ever read.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (x_dtype) {
     case PS_F16:
       return launch_normalize<__half>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
-                                      partial, chunks, st->sms, s);
+                                      partial, chunks, ce, st->sms, s);
     case PS_BF16:
       return launch_normalize<__nv_bfloat16>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p,
-                                             cols_p, partial, chunks, st->sms, s);
+                                             cols_p, partial, chunks, ce, st->sms, s);
     case PS_F32:
       return launch_normalize<float>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
-                                     partial, chunks, st->sms, s);
+                                     partial, chunks, ce, st->sms, s);
     default:
       return launch_normalize<double>(x, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
-                                      partial, chunks, st->sms, s);
+                                      partial, chunks, ce, st->sms, s);
   }
 }
 

@@ -1,8 +1,9 @@
 // HBM-bound helper kernels of the circuit:
 //   * Frobenius normalisation  Xh = fp16( fp32(X) / (||fp32(X)||_F + eps) )
 //     (polar_switch/__init__.py:34-35), two passes: per-chunk sums of squares
-//     into a caller-provided scratch array, then a scale + cast pass that also
-//     zero-fills any alignment padding;
+//     into a caller-provided scratch array (contiguous input over fixed
+//     chunks, so a matrix normalises to the same bits in any batch), then a
+//     scale + cast pass that also zero-fills any alignment padding;
 //   * copy-out of a padded FP16 result into the caller's dtype and shape
 //     (polar_switch/__init__.py:168, `.to(X.dtype).reshape(X.shape)`);
 //   * Q = Z + a*I for Gram Newton-Schulz (polar_switch/gram_newton_schulz.py:107),
@@ -85,59 +86,103 @@ __device__ __forceinline__ bool is_aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// ---------------------------------------------------------------- canonical reduction
+// The sum of squares of a contiguous matrix of E elements is reduced over
+// fixed chunks of norm_chunk_elems(E) elements, a function of E alone, so the
+// result does not depend on the batch around the matrix: per chunk, each
+// thread accumulates in FP32 the 16-byte vectors tid, tid + NORM_THREADS, ...
+// (a few dozen terms), then a fixed FP64 tree over the block; per matrix, lane
+// i of one warp sums chunks i, i + 32, ... in FP64, then a fixed shuffle tree.
+constexpr int NORM_CHUNK = 12288;       // elements per chunk (48 KB of FP32)
+constexpr int NORM_MAX_CHUNKS = 1024;   // chunks per matrix at most
+
+__host__ __device__ inline long long norm_chunk_elems(long long E) {
+  const long long nch = (E + NORM_CHUNK - 1) / NORM_CHUNK;
+  long long mult = (nch + NORM_MAX_CHUNKS - 1) / NORM_MAX_CHUNKS;
+  if (mult < 1) mult = 1;
+  return NORM_CHUNK * mult;
+}
+
+// Sum of squares of n contiguous elements (valid in thread 0). 16-byte vector
+// loads, eight in flight per thread, need an aligned start; an unaligned run
+// is read element by element in the same order, so the sum is the same.
+template <typename T>
+__device__ __forceinline__ double chunk_sumsq(const T* p, long long n, double* s_warp) {
+  constexpr int VW = Vec16<T>::VW;
+  float a = 0.f;
+  const long long nvec = n / VW;
+  if (is_aligned16(p)) {
+    long long v = threadIdx.x;
+    for (; v + 7 * NORM_THREADS < nvec; v += 8 * NORM_THREADS) {
+      float f[8][VW];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) Vec16<T>::load(p + (v + k * NORM_THREADS) * VW, f[k]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int i = 0; i < VW; ++i) a = fmaf(f[k][i], f[k][i], a);
+    }
+    for (; v < nvec; v += NORM_THREADS) {
+      float f[VW];
+      Vec16<T>::load(p + v * VW, f);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) a = fmaf(f[i], f[i], a);
+    }
+  } else {
+    for (long long v = threadIdx.x; v < nvec; v += NORM_THREADS) {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
+        const float f = to_f32(p[v * VW + i]);
+        a = fmaf(f, f, a);
+      }
+    }
+  }
+  for (long long e = nvec * VW + threadIdx.x; e < n; e += NORM_THREADS) {
+    const float f = to_f32(p[e]);
+    a = fmaf(f, f, a);
+  }
+  return block_sum(static_cast<double>(a), s_warp);
+}
+
+// Denominator of one matrix from its `nch` chunk sums; called by one full
+// warp, valid in every lane. Loads run ahead of the (ordered) additions.
+__device__ __forceinline__ float norm_den(const double* partial_m, int nch, float eps) {
+  const int lane = threadIdx.x & 31;
+  double s = 0.0;
+  int i = lane;
+  for (; i + 32 * 7 < nch; i += 32 * 8) {
+    double v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = partial_m[i + 32 * k];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += v[k];
+  }
+  for (; i < nch; i += 32) s += partial_m[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float nrm = static_cast<float>(sqrt(s));
+  return nrm + eps;  // FP32 add, as X.norm(...) + epsilon
+}
+
 // Pass 1: partial[l * chunks + chunk] = sum of squares of one chunk of matrix l.
-// `flat` means the matrix is one contiguous run of R*C elements.
+// Contiguous matrices (`flat`) use the canonical chunks of `chunk_elems`
+// elements; strided ones are split into `chunks` row ranges.
 template <typename T>
 __global__ void __launch_bounds__(NORM_THREADS)
     ps_norm_partial_kernel(const T* __restrict__ x, long long R, long long C, long long sL,
-                           long long sR, long long sC, int flat, int chunks,
+                           long long sR, long long sC, int flat, int chunks, long long chunk_elems,
                            double* __restrict__ partial) {
   __shared__ double s_warp[NORM_THREADS / 32];
   const int l = blockIdx.y, chunk = blockIdx.x;
   const T* xm = x + static_cast<long long>(l) * sL;
-  double acc = 0.0;
+  double tot;
   if (flat) {
-    constexpr int VW = Vec16<T>::VW;
     const long long E = R * C;
-    // chunk boundaries on whole 16-byte vectors
-    long long per = (E + chunks - 1) / chunks;
-    per = (per + VW - 1) / VW * VW;
-    const long long beg = chunk * per;
-    const long long end = beg + per < E ? beg + per : E;
-    if (is_aligned16(xm) && beg < end) {
-      // FP32 partial sums per thread (a few hundred terms), FP64 across threads.
-      float a0 = 0.f, a1 = 0.f;
-      const long long nvec = (end - beg) / VW;
-      const T* base = xm + beg;
-      long long v = threadIdx.x;
-      for (; v + NORM_THREADS < nvec; v += 2 * NORM_THREADS) {
-        float f0[VW], f1[VW];
-        Vec16<T>::load(base + v * VW, f0);
-        Vec16<T>::load(base + (v + NORM_THREADS) * VW, f1);
-#pragma unroll
-        for (int i = 0; i < VW; ++i) {
-          a0 = fmaf(f0[i], f0[i], a0);
-          a1 = fmaf(f1[i], f1[i], a1);
-        }
-      }
-      for (; v < nvec; v += NORM_THREADS) {
-        float f0[VW];
-        Vec16<T>::load(base + v * VW, f0);
-#pragma unroll
-        for (int i = 0; i < VW; ++i) a0 = fmaf(f0[i], f0[i], a0);
-      }
-      for (long long e = beg + nvec * VW + threadIdx.x; e < end; e += NORM_THREADS) {
-        const float f = to_f32(xm[e]);
-        a1 = fmaf(f, f, a1);
-      }
-      acc = static_cast<double>(a0) + static_cast<double>(a1);
-    } else {
-      for (long long e = beg + threadIdx.x; e < end; e += NORM_THREADS) {
-        const float v = to_f32(xm[e]);
-        acc += static_cast<double>(v) * v;
-      }
-    }
+    const long long beg = chunk * chunk_elems;
+    const long long n = beg < E ? (E - beg < chunk_elems ? E - beg : chunk_elems) : 0;
+    tot = chunk_sumsq(xm + beg, n, s_warp);
   } else {
+    double acc = 0.0;
     const long long per = (R + chunks - 1) / chunks;
     const long long rbeg = chunk * per;
     const long long rend = rbeg + per < R ? rbeg + per : R;
@@ -147,9 +192,33 @@ __global__ void __launch_bounds__(NORM_THREADS)
         acc += static_cast<double>(v) * v;
       }
     }
+    tot = block_sum(acc, s_warp);
   }
-  const double tot = block_sum(acc, s_warp);
   if (threadIdx.x == 0) partial[static_cast<long long>(l) * chunks + chunk] = tot;
+}
+
+// 8 consecutive elements of T (16-byte aligned) as floats.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
+  constexpr int VW = Vec16<T>::VW;
+  if constexpr (VW >= 8) {
+    Vec16<T>::load(p, f);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8 / VW; ++k) {
+      float g[VW];
+      Vec16<T>::load(p + k * VW, g);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) f[k * VW + i] = g[i];
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 scale8(const float (&f)[8], float den) {
+  return make_uint4(pack_half2(__fdiv_rn(f[0], den), __fdiv_rn(f[1], den)),
+                    pack_half2(__fdiv_rn(f[2], den), __fdiv_rn(f[3], den)),
+                    pack_half2(__fdiv_rn(f[4], den), __fdiv_rn(f[5], den)),
+                    pack_half2(__fdiv_rn(f[6], den), __fdiv_rn(f[7], den)));
 }
 
 // Pass 2: Xh[l] (Rp x Cp, FP16, zero padding) = X[l] / (norm_l + eps).
@@ -162,43 +231,34 @@ __global__ void __launch_bounds__(NORM_THREADS)
   __shared__ float s_den;
   const int l = blockIdx.y;
   if (threadIdx.x < 32) {
-    double s = 0.0;
-    for (int i = threadIdx.x; i < chunks; i += 32) s += partial[static_cast<long long>(l) * chunks + i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (threadIdx.x == 0) {
-      const float nrm = static_cast<float>(sqrt(s));
-      s_den = nrm + eps;  // FP32 add, as X.norm(...) + epsilon
-    }
+    const float den = norm_den(partial + static_cast<long long>(l) * chunks, chunks, eps);
+    if (threadIdx.x == 0) s_den = den;
   }
   __syncthreads();
   const float den = s_den;
   const T* xm = x + static_cast<long long>(l) * sL;
   __half* out = xh + static_cast<long long>(l) * Rp * Cp;
   if (flat && Rp == R && Cp == C) {
-    constexpr int VW = Vec16<T>::VW;
     const long long E = R * C;
     const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
     long long tail = 0;
     if (is_aligned16(xm) && is_aligned16(out)) {
-      const long long nvec = E / VW;
-      for (long long v = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; v < nvec;
-           v += stride) {
-        float f[VW];
-        Vec16<T>::load(xm + v * VW, f);
-        uint32_t h[VW / 2];
-#pragma unroll
-        for (int i = 0; i < VW / 2; ++i)
-          h[i] = pack_half2(__fdiv_rn(f[2 * i], den), __fdiv_rn(f[2 * i + 1], den));
-        if constexpr (VW == 8) {
-          *reinterpret_cast<uint4*>(out + v * VW) = make_uint4(h[0], h[1], h[2], h[3]);
-        } else if constexpr (VW == 4) {
-          *reinterpret_cast<uint2*>(out + v * VW) = make_uint2(h[0], h[1]);
-        } else {
-          *reinterpret_cast<uint32_t*>(out + v * VW) = h[0];
-        }
+      // 8 elements per 16-byte store, two groups in flight per thread.
+      const long long n8 = E / 8;
+      long long v = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x;
+      for (; v + stride < n8; v += 2 * stride) {
+        float f0[8], f1[8];
+        load8(xm + v * 8, f0);
+        load8(xm + (v + stride) * 8, f1);
+        *reinterpret_cast<uint4*>(out + v * 8) = scale8(f0, den);
+        *reinterpret_cast<uint4*>(out + (v + stride) * 8) = scale8(f1, den);
       }
-      tail = nvec * VW;
+      for (; v < n8; v += stride) {
+        float f[8];
+        load8(xm + v * 8, f);
+        *reinterpret_cast<uint4*>(out + v * 8) = scale8(f, den);
+      }
+      tail = n8 * 8;
     }
     for (long long e = tail + static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < E;
          e += stride)

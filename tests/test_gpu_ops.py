@@ -114,13 +114,31 @@ def test_apply_widened_output(cuda_device, out_dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16, torch.float64])
-@pytest.mark.parametrize("shape", [(3, 64, 96), (1, 1000, 24), (2, 7, 5)])
+@pytest.mark.parametrize("shape", [(3, 64, 96), (1, 1000, 24), (2, 7, 5), (2, 1024, 3072), (5, 200, 1152)])
 def test_normalize(cuda_device, dtype, shape):
     from polar_switch import cuda_ops
     X = seeded(shape, 80, dtype=dtype, scale=3.0)
     got = cuda_ops.normalize(X.to(cuda_device), 1e-7)
     ref = oc.normalize(X, 1e-7)
     assert_fp16_close(got, ref, max_ulps=1, max_mismatch=0.01, what=f"normalize {dtype} {shape}")
+
+
+@pytest.mark.parametrize("dtype,shape", [(torch.float32, (3, 1024, 3072)), (torch.float16, (4, 1152, 1024)),
+                                         (torch.bfloat16, (3, 384, 520)), (torch.float64, (2, 768, 768)),
+                                         (torch.float32, (2, 4096, 4096))])
+def test_normalize_is_batch_independent(cuda_device, dtype, shape):
+    """Contiguous matrices are reduced over fixed chunks, so a slice of a batch
+    normalises to exactly the bits of the same matrices in the whole batch
+    (the sharded Muon step relies on this to match a single process)."""
+    from polar_switch import cuda_ops
+    X = seeded(shape, 82, dtype=dtype, scale=2.0).to(cuda_device)
+    whole = cuda_ops.normalize(X, 1e-7)
+    part = cuda_ops.normalize(X[1:], 1e-7)
+    one = cuda_ops.normalize(X[-1:], 1e-7)
+    assert torch.equal(part, whole[1:])
+    assert torch.equal(one, whole[-1:])
+    assert_fp16_close(whole.cpu(), oc.normalize(X.cpu(), 1e-7), max_ulps=1, max_mismatch=0.01,
+                      what=f"normalize {dtype} {shape}")
 
 
 def test_normalize_strided(cuda_device):
