@@ -260,6 +260,75 @@ def run_kernel(args):
                       "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9}), flush=True)
 
 
+# Published single-GPU medians (ms) of the reference on one B200 (its README's timing
+# heatmap): shape (batch, rows, cols) -> {method: ms}.
+PUBLISHED_MS = {
+    (1, 8192, 8192): {"PS2_55": 7.47, "PS3_55": 7.47},
+    (1, 16384, 16384): {"PS2_55": 55.7, "PS3_55": 56.0},
+    (1, 14336, 4096): {"PS2_55": 1.87, "PS3_55": 1.86},
+    (1, 28672, 8192): {"PS2_55": 13.9, "PS3_55": 14.0},
+    (1, 53248, 16384): {"PS2_55": 102.0, "PS3_55": 103.0},
+    (1, 4096, 14336): {"PS2_55": 1.86, "PS3_55": 1.88},
+    (1, 8192, 28672): {"PS2_55": 13.9, "PS3_55": 13.9},
+    (1, 16384, 53248): {"PS2_55": 102.0, "PS3_55": 103.0},
+    (64, 4096, 4096): {"PS2_55": 59.8, "PS3_55": 59.4},
+    (216, 7168, 2048): {"PS2_55": 55.7, "PS3_55": 55.0},
+    (128, 8192, 1024): {"PS2_55": 9.70, "PS3_55": 9.42},
+    (216, 2048, 7168): {"PS2_55": 55.9, "PS3_55": 54.1},
+    (128, 1024, 8192): {"PS2_55": 9.72, "PS3_55": 9.34},
+}
+
+
+def run_sweep(args):
+    """--sweep: median latency of whole circuits on the shapes whose reference
+    latency is published, one JSON line per (shape, method). Inputs are FP16
+    N(0,1) (the kernels have no data-dependent paths); at least --steps timed
+    calls each after --warmup, every call timed alone with CUDA events."""
+    from polar_switch import circuit_flops, coefficients, make_polynomial_orthogonalizer
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device).manual_seed(0)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = peaks.get("bf16_tflops", 1590.0)
+    for shape, pub in PUBLISHED_MS.items():
+        X = torch.randn(shape, generator=g, device=device, dtype=torch.float16)
+        for method in ("PS2_55", "PS3_55"):
+            polar = make_polynomial_orthogonalizer(method)
+            flops = shape[0] * circuit_flops(getattr(coefficients, method), shape[1], shape[2])
+            # Warm up by time as well as by count: clocks take a while to settle
+            # after the previous (possibly power-capped) shape.
+            t_end = time.time() + 0.5
+            for i in range(max(args.warmup, 1000)):
+                polar(X)
+                torch.cuda.synchronize()
+                if i + 1 >= args.warmup and time.time() > t_end:
+                    break
+            times = []
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(0) as clocks:
+                for _ in range(args.steps):
+                    s.record()
+                    polar(X)
+                    e.record()
+                    e.synchronize()
+                    times.append(s.elapsed_time(e))
+            times.sort()
+            ms = times[len(times) // 2]
+            print(json.dumps({"shape": list(shape), "method": method, "median_ms": round(ms, 4),
+                              "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                              "frac_of_measured_burst_peak": round(flops / (ms * 1e-3) / 1e12 / peak, 3),
+                              "published_ms": pub[method],
+                              "speedup_vs_published": round(pub[method] / ms, 3),
+                              "clocks": clocks.summary()}), flush=True)
+        del X
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -281,7 +350,12 @@ def main():
                     help="multi-GPU: cap on GEMM CTAs, leaving SMs to the all-gather")
     ap.add_argument("--transport", default="auto", choices=["auto", "copy_engine", "collective"],
                     help="multi-GPU: copy-engine pushes into symmetric memory, or the NCCL all-gather")
+    ap.add_argument("--sweep", action="store_true",
+                    help="median circuit latency on every shape with a published reference latency")
     args = ap.parse_args()
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.kernel:
         run_kernel(args)
         return

@@ -72,21 +72,63 @@ struct GemmArgs {
   long long wait_limit;      // cycles before a bounded wait gives up
 };
 
+// Symmetric tiles: row block bi owns the tiles starting at block columns
+// j = bi, bi + 2, ... < tb (each tile covers blocks j and j + 1). They are
+// visited in bands of SYM_BAND row blocks; inside a band by start column j,
+// and for each j by row. CTAs that run at the same time then share a few A row
+// panels and B column panels, so a long K streams each panel from DRAM about
+// once per band instead of once per tile.
+constexpr int SYM_BAND = 16;
+
+// Rows x in [lo, hi) with x % 2 == par.
+__device__ __forceinline__ int count_parity(int lo, int hi, int par) {
+  return ((hi - par + 1) >> 1) - ((lo - par + 1) >> 1);
+}
+
+__device__ __forceinline__ void decode_sym(int tb, int r, int& bi, int& j) {
+  int lo = 0, hi = 0;
+  while (true) {
+    hi = min(lo + SYM_BAND, tb);
+    int total = 0;
+    for (int x = lo; x < hi; ++x) total += (tb - x + 1) >> 1;
+    if (r < total) break;
+    r -= total;
+    lo = hi;
+  }
+  // Start columns inside the band: the count of rows grows with j ...
+  for (j = lo; j < tb; ++j) {
+    const int par = j & 1;
+    const int cnt = count_parity(lo, min(hi, j + 1), par);
+    if (r < cnt) {
+      bi = lo + ((lo & 1) != par) + 2 * r;
+      return;
+    }
+    r -= cnt;
+    if (j >= hi - 1) break;
+  }
+  // ... and from j = hi on alternates between the band's even and odd rows.
+  ++j;
+  const int ce = count_parity(lo, hi, 0), co = count_parity(lo, hi, 1);
+  const int k = r / (ce + co);
+  j += 2 * k;
+  r -= k * (ce + co);
+  const int c_first = (j & 1) ? co : ce;
+  if (r >= c_first) {
+    r -= c_first;
+    ++j;
+  }
+  bi = lo + ((lo & 1) != (j & 1)) + 2 * r;
+}
+
 template <bool SYM>
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& b, int& m0, int& n0) {
   b = t / a.tiles_per_mat;
   int r = t - b * a.tiles_per_mat;
   if (SYM) {
-    // Row bi owns ceil((tb - bi) / 2) tiles starting at block column bi.
-    int bi = 0;
-    while (true) {
-      const int cnt = (a.tb - bi + 1) >> 1;
-      if (r < cnt) break;
-      r -= cnt;
-      ++bi;
-    }
+    int bi, j;
+    decode_sym(a.tb, r, bi, j);
     m0 = bi * BM;
-    n0 = (bi + 2 * r) * BM;
+    n0 = j * BM;
   } else {
     const int per_group = a.group_m * a.tiles_n;
     const int g = r / per_group;
