@@ -317,40 +317,141 @@ int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& ta2,
   return PS_OK;
 }
 
+// A GEMM prepared but not yet launched: its maps and arguments, its profiling
+// figures, and the launcher of its kernel variant. Jobs of one variant and
+// profiling kind can share a launch (ps::GemmBatch).
+struct GemmJob;
+using JobLauncher = int (*)(const GemmJob* jobs, int n, cudaStream_t stream);
+struct GemmJob {
+  ps::GemmProblem prob;
+  JobLauncher launch;
+  int variant, kind;
+  double flops, bytes;
+};
+
+// While a sink is installed on this thread, launch_gemm collects jobs instead
+// of launching them; flush_jobs then launches them batched.
+thread_local std::vector<GemmJob>* g_job_sink = nullptr;
+
+template <bool A_MN, bool B_MN, bool SYM, int OUT>
+int launch_jobs(const GemmJob* jobs, int n, cudaStream_t stream) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const int variant = jobs[0].variant;
+  if (g_use_pair) {
+    for (int i = 0; i < n; ++i) {
+      const ps::GemmProblem& q = jobs[i].prob;
+      if ((rc = launch_gemm_pair<A_MN, B_MN, SYM, OUT>(variant, q.tmA, q.tmA2, q.tmB, q.tmB2, q.tmD,
+                                                        to_pair(q.args, SYM), stream, st,
+                                                        jobs[i].kind, jobs[i].flops, jobs[i].bytes)))
+        return rc;
+    }
+    return PS_OK;
+  }
+  auto kern1 = ps::ps_gemm_kernel<A_MN, B_MN, SYM, OUT, false>;
+  auto kernb = ps::ps_gemm_kernel<A_MN, B_MN, SYM, OUT, true>;
+  if (!st->smem_attr[variant]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize, ps::SMEM_TOTAL);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(kernb, cudaFuncAttributeMaxDynamicSharedMemorySize, ps::SMEM_TOTAL);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm smem)");
+    st->smem_attr[variant] = true;
+  }
+  for (int i0 = 0; i0 < n; i0 += ps::MAX_BATCH) {
+    const int cnt = n - i0 < ps::MAX_BATCH ? n - i0 : ps::MAX_BATCH;
+    ps::GemmBatch batch;
+    std::memset(&batch, 0, sizeof(batch));
+    double flops = 0.0, bytes = 0.0;
+    int total = 0, used = 0;
+    for (int i = 0; i < cnt; ++i) {
+      const GemmJob& j = jobs[i0 + i];
+      if (j.prob.args.total_tiles <= 0) continue;
+      batch.p[used] = j.prob;
+      batch.p[used].args.status = st->status;
+      batch.p[used].args.wait_limit = g_wait_limit;
+      batch.tile_start[used] = total;
+      total += j.prob.args.total_tiles;
+      flops += j.flops;
+      bytes += j.bytes;
+      ++used;
+    }
+    if (used == 0) continue;
+    batch.count = used;
+    batch.tile_start[used] = total;
+    int grid = total < st->sms ? total : st->sms;
+    if (g_max_ctas > 0 && grid > g_max_ctas) grid = g_max_ctas;
+    LaunchScope scope(jobs[i0].kind, stream, flops, bytes);
+    if (used == 1)
+      kern1<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(batch);
+    else
+      kernb<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(batch);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  }
+  return PS_OK;
+}
+
+// Launches collected jobs: jobs of one variant and kind share launches (they
+// are independent, so their order does not matter).
+int flush_jobs(std::vector<GemmJob>& jobs, cudaStream_t stream) {
+  std::vector<bool> done(jobs.size(), false);
+  std::vector<GemmJob> group;
+  for (size_t i = 0; i < jobs.size(); ++i) {
+    if (done[i]) continue;
+    group.clear();
+    for (size_t k = i; k < jobs.size(); ++k) {
+      if (!done[k] && jobs[k].launch == jobs[i].launch && jobs[k].kind == jobs[i].kind) {
+        group.push_back(jobs[k]);
+        done[k] = true;
+      }
+    }
+    const int rc = jobs[i].launch(group.data(), static_cast<int>(group.size()), stream);
+    if (rc) return rc;
+  }
+  jobs.clear();
+  return PS_OK;
+}
+
+// Installs a job sink for the current scope (see g_job_sink).
+struct JobSink {
+  std::vector<GemmJob> jobs;
+  std::vector<GemmJob>* prev;
+  JobSink() : prev(g_job_sink) { g_job_sink = &jobs; }
+  ~JobSink() { g_job_sink = prev; }
+  int flush(cudaStream_t s) {
+    g_job_sink = prev;
+    return flush_jobs(jobs, s);
+  }
+};
+
 // ta2 / tb2: the operands' maps in the other majorness, read only when the
-// operand is triangle-stored (args.a_tri / b_tri, CTA-pair kernel only).
+// operand is triangle-stored (args.a_tri / b_tri).
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
 int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                 ps::GemmArgs args, cudaStream_t stream, int kind, double flops, double bytes,
                 const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
-  DeviceState* st = nullptr;
-  int rc = device_state(&st);
-  if (rc) return rc;
   if ((args.a_tri && !ta2) || (args.b_tri && !tb2))
     return fail(PS_ERR_INVALID, "internal: triangle-stored operand without its second map");
-  if (g_use_pair)
-    return launch_gemm_pair<A_MN, B_MN, SYM, OUT>(variant, ta, ta2 ? *ta2 : ta, tb,
-                                                  tb2 ? *tb2 : tb, td, to_pair(args, SYM), stream,
-                                                  st, kind, flops, bytes);
-
-  auto kern = ps::ps_gemm_kernel<A_MN, B_MN, SYM, OUT>;
-  if (!st->smem_attr[variant]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, ps::SMEM_TOTAL);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm smem)");
-    st->smem_attr[variant] = true;
+  GemmJob job;
+  std::memset(&job, 0, sizeof(job));
+  job.prob.tmA = ta;
+  job.prob.tmA2 = ta2 ? *ta2 : ta;
+  job.prob.tmB = tb;
+  job.prob.tmB2 = tb2 ? *tb2 : tb;
+  job.prob.tmD = td;
+  job.prob.args = args;
+  job.launch = &launch_jobs<A_MN, B_MN, SYM, OUT>;
+  job.variant = variant;
+  job.kind = kind;
+  job.flops = flops;
+  job.bytes = bytes;
+  if (g_job_sink) {
+    g_job_sink->push_back(job);
+    return PS_OK;
   }
-  if (args.total_tiles <= 0) return PS_OK;
-  args.status = st->status;
-  args.wait_limit = g_wait_limit;
-  int grid = args.total_tiles < st->sms ? args.total_tiles : st->sms;
-  if (g_max_ctas > 0 && grid > g_max_ctas) grid = g_max_ctas;
-  LaunchScope scope(kind, stream, flops, bytes);
-  kern<<<grid, ps::NUM_THREADS, ps::SMEM_TOTAL, stream>>>(ta, ta2 ? *ta2 : ta, tb,
-                                                           tb2 ? *tb2 : tb, td, args);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
-  return PS_OK;
+  return launch_jobs<A_MN, B_MN, SYM, OUT>(&job, 1, stream);
 }
 
 void fill_sym_tiles(ps::GemmArgs& a, int64_t n, int64_t L) {
@@ -999,11 +1100,16 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
   }
   int off = 0;
   for (int t = 0; t < n_outer; ++t) {
-    for (int i = 0; i < np; ++i) {
-      const GroupedPlan::Prob& p = plan.probs[i];
-      if ((rc = gram_impl(ws + p.xh_off[cur[i]], buf_ptr(i, 0), probs[i].L, p.lay.Rp, p.lay.Cp,
-                          p.lay.Cp, p.lay.tall, s, tri)))
-        return rc;
+    // The Grams of all problems, batched into one launch per kernel variant.
+    {
+      JobSink sink;
+      for (int i = 0; i < np; ++i) {
+        const GroupedPlan::Prob& p = plan.probs[i];
+        if ((rc = gram_impl(ws + p.xh_off[cur[i]], buf_ptr(i, 0), probs[i].L, p.lay.Rp, p.lay.Cp,
+                            p.lay.Cp, p.lay.tall, s, tri)))
+          return rc;
+      }
+      if ((rc = sink.flush(s))) return rc;
     }
     int last = 0;
     for (int k = 0; k < n_steps[t]; ++k) {
@@ -1020,6 +1126,8 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
     }
     off += n_steps[t];
     const bool final_iter = t == n_outer - 1;
+    // The applies of all problems, batched likewise.
+    JobSink sink;
     for (int i = 0; i < np; ++i) {
       const GroupedPlan::Prob& p = plan.probs[i];
       const ps_problem& q = probs[i];
@@ -1034,6 +1142,7 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
       }
       if (rc) return rc;
     }
+    if ((rc = sink.flush(s))) return rc;
   }
   for (int i = 0; i < np; ++i) {
     if (direct[i]) continue;

@@ -4,7 +4,7 @@
 //   symmetric  D = alpha * A . B^T + beta * C + diag * I     (gram, square,
 //              only tiles on or above the block diagonal are computed; the
 //              epilogue writes each off-diagonal 128x128 block twice, once
-//              transposed)
+//              transposed, unless the result is kept as upper-triangle blocks)
 //   general    D = A . B^T + beta * C                          (apply)
 //
 // "B^T" is in the UMMA sense (B supplies N rows of K): a K-major B tile is
@@ -17,11 +17,13 @@
 // TMEM, and the epilogue does alpha/beta*C/diag in FP32 followed by exactly
 // one rounding to FP16 (optionally widened to FP32/BF16 for the final output).
 //
-// Roles (192 threads, one CTA per SM, persistent over a static tile list):
+// Roles (320 threads, one CTA per SM, persistent over a static tile list that
+// may span several problems, see GemmBatch):
 //   warp 0 lane 0   TMA producer, STAGES-deep smem ring
 //   warp 1          TMEM allocator; lane 0 issues the UMMAs
-//   warps 2..5      epilogue: tcgen05.ld -> FP32 math -> swizzled smem ->
-//                   TMA store (plus the mirrored store for symmetric tiles)
+//   warps 2..9      epilogue, two warps per TMEM lane quarter, 128 columns
+//                   each: tcgen05.ld -> FP32 math -> swizzled smem -> TMA
+//                   store (plus the mirrored store for symmetric tiles)
 //
 // Reference behaviour this follows: polar_switch/triton_kernels.py:24-57 (one
 // owner per symmetric tile, FP32 epilogue alpha*acc + beta*C then + diag,
@@ -65,20 +67,24 @@ struct GemmArgs {
   const __half* C;           // addend (FP16), may alias D in symmetric mode
   long long c_ld, c_bs;      // addend leading dimension / batch stride (elements)
   int has_addend, has_diag;
-  // Triangle storage, honoured by the CTA-pair kernel only (see ps_gemm2.cuh);
-  // this kernel always stores full symmetric results.
+  // Triangle storage: a_tri / b_tri mark operands held as upper-triangle
+  // blocks (read through the second maps, see tri_transposed); store_mirror = 0
+  // keeps a symmetric result that way (no transposed stores).
   int a_tri, b_tri, store_mirror;
   int* status;               // device status word
   long long wait_limit;      // cycles before a bounded wait gives up
 };
 
 // Symmetric tiles: row block bi owns the tiles starting at block columns
-// j = bi, bi + 2, ... < tb (each tile covers blocks j and j + 1). They are
-// visited in bands of SYM_BAND row blocks; inside a band by start column j,
-// and for each j by row. CTAs that run at the same time then share a few A row
+// j = bi, bi + 2, ... < tb (each tile covers blocks j and j + 1). Above
+// SYM_BAND row blocks they are visited in bands of SYM_BAND row blocks; inside
+// a band by start column j, and for each j by row. CTAs that run at the same time then share a few A row
 // panels and B column panels, so a long K streams each panel from DRAM about
 // once per band instead of once per tile.
-constexpr int SYM_BAND = 16;
+#ifndef PS_SYM_BAND
+#define PS_SYM_BAND 16
+#endif
+constexpr int SYM_BAND = PS_SYM_BAND;
 
 // Rows x in [lo, hi) with x % 2 == par.
 __device__ __forceinline__ int count_parity(int lo, int hi, int par) {
@@ -120,13 +126,54 @@ __device__ __forceinline__ void decode_sym(int tb, int r, int& bi, int& j) {
   bi = lo + ((lo & 1) != (j & 1)) + 2 * r;
 }
 
+// One launch covers up to MAX_BATCH problems of the same kernel variant (same
+// operand majorness, symmetry and output type): their tiles are numbered one
+// after the other (tile_start), and each tile reads its problem's maps and
+// arguments. Circuits use this to run the Gram or apply of every bucket of a
+// grouped call as one persistent launch.
+#ifndef PS_MAX_BATCH
+#define PS_MAX_BATCH 8
+#endif
+constexpr int MAX_BATCH = PS_MAX_BATCH;
+
+struct alignas(64) GemmProblem {
+  // tmA / tmB: boxes in the operand's native majorness (A_MN / B_MN);
+  // tmA2 / tmB2: the other majorness, read only for triangle-stored operands.
+  CUtensorMap tmA, tmA2, tmB, tmB2, tmD;
+  GemmArgs args;
+};
+
+struct GemmBatch {
+  GemmProblem p[MAX_BATCH];
+  int tile_start[MAX_BATCH + 1];
+  int count;
+};
+
+__device__ __forceinline__ int batch_problem(const GemmBatch& batch, int t) {
+  int pi = 0;
+  while (pi + 1 < batch.count && t >= batch.tile_start[pi + 1]) ++pi;
+  return pi;
+}
+
 template <bool SYM>
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& b, int& m0, int& n0) {
   b = t / a.tiles_per_mat;
   int r = t - b * a.tiles_per_mat;
   if (SYM) {
-    int bi, j;
-    decode_sym(a.tb, r, bi, j);
+    int bi = 0, j;
+    if (a.tb <= SYM_BAND) {
+      // One band: plain row order, the cheapest decode (it sits on the UMMA
+      // issuer's path between tiles, which matters when K is short).
+      while (true) {
+        const int cnt = (a.tb - bi + 1) >> 1;
+        if (r < cnt) break;
+        r -= cnt;
+        ++bi;
+      }
+      j = bi + 2 * r;
+    } else {
+      decode_sym(a.tb, r, bi, j);
+    }
     m0 = bi * BM;
     n0 = j * BM;
   } else {
@@ -188,13 +235,12 @@ __device__ __forceinline__ void convert_row(const float (&f)[32], uint32_t (&w)[
   }
 }
 
-template <bool A_MN, bool B_MN, bool SYM, int OUT>
+// BATCHED = false: batch.count is 1 and the problem index is the constant 0, so
+// the arguments are read at fixed parameter offsets (as cheap as plain kernel
+// parameters); BATCHED = true looks the problem up per tile.
+template <bool A_MN, bool B_MN, bool SYM, int OUT, bool BATCHED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    ps_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
-                   const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB2,
-                   const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
-  // tmA / tmB: boxes in the operand's native majorness (A_MN / B_MN);
-  // tmA2 / tmB2: the other majorness, read only for triangle-stored operands.
+    ps_gemm_kernel(const __grid_constant__ GemmBatch batch) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms.
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -226,11 +272,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-    tma_prefetch_desc(&tmD);
-    if (args.a_tri) tma_prefetch_desc(&tmA2);
-    if (args.b_tri) tma_prefetch_desc(&tmB2);
+    for (int pi = 0; pi < batch.count; ++pi) {
+      const GemmProblem& P = batch.p[pi];
+      tma_prefetch_desc(&P.tmA);
+      tma_prefetch_desc(&P.tmB);
+      tma_prefetch_desc(&P.tmD);
+      if (P.args.a_tri) tma_prefetch_desc(&P.tmA2);
+      if (P.args.b_tri) tma_prefetch_desc(&P.tmB2);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -241,8 +290,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_kb = (args.K + BK - 1) / BK;
-  const int ncols_total = args.N;  // symmetric: N == M
+  const int total_tiles = batch.tile_start[batch.count];
+  int* const status = batch.p[0].args.status;          // the same for every problem
+  const long long wait_limit = batch.p[0].args.wait_limit;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -251,12 +301,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const int pi = BATCHED ? batch_problem(batch, t) : 0;
+        const GemmProblem& P = batch.p[pi];
+        const GemmArgs& args = P.args;
+        const int num_kb = (args.K + BK - 1) / BK;
         int b, m0, n0;
-        decode_tile<SYM>(args, t, b, m0, n0);
+        decode_tile<SYM>(args, t - batch.tile_start[pi], b, m0, n0);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status,
-                                 kStatusProducerTimeout, args.wait_limit)) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status,
+                                 kStatusProducerTimeout, wait_limit)) {
             ok = false;
             break;
           }
@@ -267,8 +321,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int kb128 = k0 / BM;
           const bool at = args.a_tri && tri_transposed(A_MN, m0 / BM, m0 / BM, kb128);
           const bool bt = args.b_tri && tri_transposed(B_MN, n0 / BM, n0 / BM + 1, kb128);
-          const CUtensorMap* ma = at ? &tmA2 : &tmA;
-          const CUtensorMap* mb = bt ? &tmB2 : &tmB;
+          const CUtensorMap* ma = at ? &P.tmA2 : &P.tmA;
+          const CUtensorMap* mb = bt ? &P.tmB2 : &P.tmB;
           if (A_MN == at) {  // K-major tile
             tma_load_3d(ma, a_dst, &full[stage], k0, m0, b);
           } else {
@@ -298,8 +352,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t par = (issued_parity >> s) & 1u;
           const long long start = clock64();
           while (!mbar_try_wait(&full[s], par)) {
-            if (clock64() - start > args.wait_limit) {
-              if (args.status) atomicCAS(args.status, 0, kStatusDrainTimeout);
+            if (clock64() - start > wait_limit) {
+              if (status) atomicCAS(status, 0, kStatusDrainTimeout);
               break;
             }
           }
@@ -315,22 +369,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const int pi = BATCHED ? batch_problem(batch, t) : 0;
+        const GemmProblem& P = batch.p[pi];
+        const GemmArgs& args = P.args;
+        const int num_kb = (args.K + BK - 1) / BK;
+        const int ncols_total = args.N;  // symmetric: N == M
         int b, m0, n0;
-        decode_tile<SYM>(args, t, b, m0, n0);
+        decode_tile<SYM>(args, t - batch.tile_start[pi], b, m0, n0);
         int nvalid = ncols_total - n0;
         nvalid = nvalid > BN ? BN : nvalid;
         const int n_mma = (nvalid + 15) & ~15;
-        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status,
-                               kStatusMmaTimeout, args.wait_limit)) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, status,
+                               kStatusMmaTimeout, wait_limit)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.status, kStatusMmaTimeout,
-                                 args.wait_limit)) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusMmaTimeout,
+                                 wait_limit)) {
             ok = false;
             break;
           }
@@ -371,8 +430,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         umma_commit(drain);
         const long long start = clock64();
         while (!mbar_try_wait(drain, 0)) {
-          if (clock64() - start > args.wait_limit) {
-            if (args.status) atomicCAS(args.status, 0, kStatusDrainTimeout);
+          if (clock64() - start > wait_limit) {
+            if (status) atomicCAS(status, 0, kStatusDrainTimeout);
             break;
           }
         }
@@ -396,9 +455,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     int slot = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const int pi = BATCHED ? batch_problem(batch, t) : 0;
+      const GemmProblem& P = batch.p[pi];
+      const GemmArgs& args = P.args;
+      const int ncols_total = args.N;  // symmetric: N == M
       int b, m0, n0;
-      decode_tile<SYM>(args, t, b, m0, n0);
+      decode_tile<SYM>(args, t - batch.tile_start[pi], b, m0, n0);
       const int c_first = 4 * h;  // this warp's chunks: c_first .. c_first + 3
       int nvalid = ncols_total - (n0 + 32 * c_first);
       nvalid = nvalid > BN / 2 ? BN / 2 : nvalid;
@@ -521,8 +584,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           if (row0 < args.M && gcol0 < ncols_total) {
-            tma_store_3d(&tmD, sb, gcol0, row0, b);
-            if (mirror) tma_store_3d(&tmD, sb + BUF_BYTES, row0, gcol0, b);
+            tma_store_3d(&P.tmD, sb, gcol0, row0, b);
+            if (mirror) tma_store_3d(&P.tmD, sb + BUF_BYTES, row0, gcol0, b);
           }
           bulk_commit();
         }
@@ -535,8 +598,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&tempty[acc]);
       };
 
-      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, args.status,
-                             kStatusEpilogueTimeout, args.wait_limit)) {
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, status,
+                             kStatusEpilogueTimeout, wait_limit)) {
         ok = false;
         break;
       }

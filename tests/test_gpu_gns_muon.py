@@ -59,6 +59,28 @@ def test_grouped_matches_single_calls(cuda_device):
         assert torch.equal(g, single)
 
 
+def test_grouped_many_buckets_batched_launches(cuda_device):
+    """More buckets than one launch takes (8 problems per launch): every
+    bucket still equals its own call bit for bit, and the Grams and applies
+    of all buckets run in a few batched launches per outer iteration."""
+    from polar_switch import _native as nat
+    from polar_switch import make_polynomial_orthogonalizer
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    shapes = [(2, 256, 128), (1, 128, 256), (2, 136, 136), (1, 384, 128), (3, 128, 128),
+              (1, 128, 512), (2, 264, 128), (1, 128, 200), (2, 520, 128), (1, 128, 640)]
+    banks = [seeded(s, 47 + i).to(cuda_device) for i, s in enumerate(shapes)]
+    nat.profile_enable(True)
+    grouped = polar.grouped(banks)
+    prof = nat.profile_read()
+    nat.profile_enable(False)
+    # 2 outer iterations; per iteration Grams: tall and wide variants (5 problems each),
+    # applies: one variant for all 10 problems -> 2 launches of 8 + 2
+    assert prof["gram"]["launches"] == 2 * 2
+    assert prof["apply"]["launches"] == 2 * 2
+    for b, g in zip(banks, grouped):
+        assert torch.equal(g, polar(b))
+
+
 def test_grouped_fp16_outputs(cuda_device):
     from polar_switch import make_polynomial_orthogonalizer
     polar = make_polynomial_orthogonalizer("PS3_55")
