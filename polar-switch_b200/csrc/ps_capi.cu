@@ -50,7 +50,13 @@ thread_local std::string g_last_error;
 long long g_wait_limit = ps::kDefaultWaitLimit;
 // GEMMs run on the one-CTA kernel unless CTA pairs (cta_group::2) are selected
 // with ps_set_cta_pairs; measured faster on every circuit shape.
-bool g_use_pair = false;
+// Which GEMM kernel runs: 0 = the one-CTA kernel, 1 = the CTA-pair kernel, 2
+// (default) = CTA pairs for squares of buffers up to kPairMaxN (where sharing
+// the B tile across the pair pays: measured 17 % faster at n = 1024), the
+// one-CTA kernel for everything else (Grams, applies and large squares run
+// faster there).
+int g_pair_mode = 2;
+constexpr int64_t kPairMaxN = 2048;
 // Upper bound on the CTAs (SMs) a persistent GEMM grid may take; 0 = all SMs.
 // Leaving SMs free lets a collective run beside the GEMMs.
 int g_max_ctas = 0;
@@ -239,7 +245,11 @@ int map_out(CUtensorMap* m, const void* p, int dtype, int64_t cols, int64_t rows
 }
 
 // Rows of the B-operand box a K-major B tile needs in the selected kernel.
-uint32_t b_box_rows() { return g_use_pair ? ps::pair::BNH : ps::BN; }
+// Whether a product of this kind on n x n buffers runs on CTA pairs.
+bool use_pair(bool square, int64_t n) {
+  return g_pair_mode == 1 || (g_pair_mode == 2 && square && n <= kPairMaxN);
+}
+uint32_t b_box_rows(bool pair) { return pair ? ps::pair::BNH : ps::BN; }
 
 // Same problem as `g`, tiled for the CTA-pair kernel.
 ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
@@ -326,6 +336,7 @@ struct GemmJob {
   ps::GemmProblem prob;
   JobLauncher launch;
   int variant, kind;
+  bool pair;  // run on the CTA-pair kernel
   double flops, bytes;
 };
 
@@ -339,7 +350,7 @@ int launch_jobs(const GemmJob* jobs, int n, cudaStream_t stream) {
   int rc = device_state(&st);
   if (rc) return rc;
   const int variant = jobs[0].variant;
-  if (g_use_pair) {
+  if (jobs[0].pair) {
     for (int i = 0; i < n; ++i) {
       const ps::GemmProblem& q = jobs[i].prob;
       if ((rc = launch_gemm_pair<A_MN, B_MN, SYM, OUT>(variant, q.tmA, q.tmA2, q.tmB, q.tmB2, q.tmD,
@@ -402,7 +413,8 @@ int flush_jobs(std::vector<GemmJob>& jobs, cudaStream_t stream) {
     if (done[i]) continue;
     group.clear();
     for (size_t k = i; k < jobs.size(); ++k) {
-      if (!done[k] && jobs[k].launch == jobs[i].launch && jobs[k].kind == jobs[i].kind) {
+      if (!done[k] && jobs[k].launch == jobs[i].launch && jobs[k].kind == jobs[i].kind &&
+          jobs[k].pair == jobs[i].pair) {
         group.push_back(jobs[k]);
         done[k] = true;
       }
@@ -431,7 +443,7 @@ struct JobSink {
 template <bool A_MN, bool B_MN, bool SYM, int OUT>
 int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                 ps::GemmArgs args, cudaStream_t stream, int kind, double flops, double bytes,
-                const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
+                bool pair, const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
   if ((args.a_tri && !ta2) || (args.b_tri && !tb2))
     return fail(PS_ERR_INVALID, "internal: triangle-stored operand without its second map");
   GemmJob job;
@@ -445,6 +457,7 @@ int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const
   job.launch = &launch_jobs<A_MN, B_MN, SYM, OUT>;
   job.variant = variant;
   job.kind = kind;
+  job.pair = pair;
   job.flops = flops;
   job.bytes = bytes;
   if (g_job_sink) {
@@ -508,9 +521,10 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   // read MN-major from its row-major storage, exactly the reference's
   // gemm_symmetric(A, B) even when B is symmetric only up to rounding.
   const bool same = p == q;
+  const bool pair = use_pair(same, n);
   if ((rc = map_kmajor(&ta, p, n, n, L, n, n * n, ps::BM))) return rc;
   if (same) {
-    if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, b_box_rows()))) return rc;
+    if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, b_box_rows(pair)))) return rc;
   } else {
     if ((rc = map_mnmajor(&tb, q, n, n, L, n, n * n))) return rc;
   }
@@ -534,13 +548,13 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
     a.a_tri = a.b_tri = 1;
     a.store_mirror = 0;
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
-                                                        L * nn * n, bytes, &tm, &tm);
+                                                        L * nn * n, bytes, pair, &tm, &tm);
   }
   if (same)
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
-                                                        L * nn * n, bytes);
+                                                        L * nn * n, bytes, pair);
   return launch_gemm<false, true, true, ps::kOutF16>(8, ta, tb, td, a, stream, kProfSquare,
-                                                     L * nn * n, bytes);
+                                                     L * nn * n, bytes, pair);
 }
 
 int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
@@ -561,27 +575,28 @@ int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, i
   a.store_mirror = tri_out ? 0 : 1;
   const double flops = static_cast<double>(L) * n * n * K;
   const double bytes = static_cast<double>(L) * 2.0 * (static_cast<double>(n) * K + n * n);
+  const bool pair = use_pair(false, n);
   if (!tall) {
     if ((rc = map_kmajor(&ta, x, K, n, L, x_ld, rows * x_ld, ps::BM))) return rc;
-    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, b_box_rows()))) return rc;
+    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, b_box_rows(pair)))) return rc;
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfGram,
-                                                        flops, bytes);
+                                                        flops, bytes, pair);
   }
   if ((rc = map_mnmajor(&ta, x, n, K, L, x_ld, rows * x_ld))) return rc;
   return launch_gemm<true, true, true, ps::kOutF16>(1, ta, ta, td, a, stream, kProfGram, flops,
-                                                    bytes);
+                                                    bytes, pair);
 }
 
 template <int OUT>
 int apply_launch(bool tall, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                 const ps::GemmArgs& a, cudaStream_t s, const CUtensorMap* t2) {
+                 const ps::GemmArgs& a, cudaStream_t s, const CUtensorMap* t2, bool pair) {
   const double M = a.M, N = a.N, K = a.K, L = a.L;
   const double out_bytes = OUT == ps::kOutF32 ? 4.0 : 2.0;
   const double flops = 2.0 * L * M * N * K;
   const double bytes = L * (2.0 * K * K + 2.0 * M * N + out_bytes * M * N);
   (void)tall;  // both orientations are A (K-major) times B (MN-major)
   return launch_gemm<false, true, false, OUT>(2 + OUT, ta, tb, td, a, s, kProfApply, flops, bytes,
-                                              a.a_tri ? t2 : nullptr, a.b_tri ? t2 : nullptr);
+                                              pair, a.a_tri ? t2 : nullptr, a.b_tri ? t2 : nullptr);
 }
 
 int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
@@ -627,17 +642,17 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
       if ((rc = map_mnmajor(&t2, b, n, n, L, n, n * n))) return rc;
       a.a_tri = 1;
     } else {
-      if ((rc = map_kmajor(&t2, b, n, n, L, n, n * n, b_box_rows()))) return rc;
+      if ((rc = map_kmajor(&t2, b, n, n, L, n, n * n, b_box_rows(use_pair(false, n))))) return rc;
       a.b_tri = 1;
     }
   }
   switch (y_dtype) {
     case PS_F16:
-      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream, &t2);
+      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream, &t2, use_pair(false, n));
     case PS_F32:
-      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream, &t2);
+      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream, &t2, use_pair(false, n));
     default:
-      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream, &t2);
+      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream, &t2, use_pair(false, n));
   }
 }
 
@@ -946,9 +961,10 @@ int ps_set_max_ctas(int max_ctas) {
   return previous;
 }
 
-int ps_set_cta_pairs(int enable) {
-  const int previous = g_use_pair ? 1 : 0;
-  g_use_pair = enable != 0;
+int ps_set_cta_pairs(int mode) {
+  if (mode < 0 || mode > 2) return fail(PS_ERR_INVALID, "ps_set_cta_pairs: mode must be 0, 1 or 2");
+  const int previous = g_pair_mode;
+  g_pair_mode = mode;
   return previous;
 }
 

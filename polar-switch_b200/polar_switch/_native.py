@@ -172,9 +172,13 @@ def profile_read():
     return out
 
 
-def set_cta_pairs(enable):
-    """Select the CTA-pair GEMM kernel (True) or the one-CTA kernel (False, default); returns the previous."""
-    return bool(load().ps_set_cta_pairs(1 if enable else 0))
+def set_cta_pairs(mode):
+    """GEMM kernel selection: 0/False one-CTA kernel, 1/True CTA pairs, 2 (default) CTA
+    pairs for squares with n <= 2048 only. Returns the previous mode (an int)."""
+    rc = load().ps_set_cta_pairs(int(mode))
+    if rc < 0:
+        check("ps_set_cta_pairs", rc)
+    return rc
 
 
 def set_max_ctas(max_ctas):
