@@ -350,6 +350,8 @@ def main():
                          "gather/compute overlap (default: auto)")
     ap.add_argument("--gemm-ctas", type=int, default=None,
                     help="multi-GPU: cap on GEMM CTAs, leaving SMs to the all-gather")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture the step as a CUDA graph once and replay it in the timed region")
     ap.add_argument("--transport", default="auto", choices=["auto", "copy_engine", "collective"],
                     help="multi-GPU: copy-engine pushes into symmetric memory, or the NCCL all-gather")
     ap.add_argument("--sweep", action="store_true",
@@ -393,18 +395,30 @@ def main():
     for _ in range(args.warmup):
         step(banks)
     barrier()
+    run_step = lambda: step(banks)  # noqa: E731
+    launches_per_step = None
+    if args.graph:
+        n0 = nat.launch_count()
+        step.capture(banks, warmup=0)
+        launches_per_step = nat.launch_count() - n0
+        run_step = step.replay
+        barrier()
 
     stream = torch.cuda.current_stream(device)
     t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = nat.launch_count()
     with ClockSampler(local) as clocks:
         barrier()
+        h0 = time.perf_counter()
         t_start.record(stream)
         for _ in range(args.steps):
-            step(banks)
+            run_step()
         t_stop.record(stream)
+        host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
         barrier()
     launches = nat.launch_count() - launches0
+    if launches_per_step is not None:
+        launches = launches_per_step * args.steps  # graph replays launch the captured kernels
     ms = t_start.elapsed_time(t_stop) / args.steps
     ms = max_over_ranks(ms, world, device)
     value = flops / (ms * 1e-3) / 1e12
@@ -491,9 +505,11 @@ def main():
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            "host_enqueue_ms_per_step": host_ms,
         }
         if world > 1:
             line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
+                                        "cuda_graph": bool(args.graph),
                                         "gemm_ctas": args.gemm_ctas,
                                         "bucket_matrices": [sum(c for _, _, c in p["pieces"]) for p in step.plans],
                                         "bytes_per_step": step.recv.numel() * 2}

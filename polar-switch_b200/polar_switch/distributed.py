@@ -346,10 +346,32 @@ class ShardedOrthogonalizer:
         self._barrier_on(comm)
         main.wait_stream(comm)
 
+    def capture(self, banks, warmup=2):
+        """Record one whole step on these bank tensors as a CUDA graph (after
+        `warmup` eager steps); `replay()` then runs it again with no host work
+        per launch. The banks must stay at the same addresses (e.g. persistent
+        momentum buffers)."""
+        if self.device.type != "cuda":
+            raise ValueError("graph capture needs CUDA tensors")
+        for _ in range(warmup):
+            self(banks)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self(banks)
+        torch.cuda.synchronize(self.device)
+        self._graph = graph
+        return graph
+
+    def replay(self):
+        """Run the captured step; returns the gathered buffer (stream-ordered)."""
+        self._graph.replay()
+        return self.recv
+
     def close(self):
         """Drop the peer mappings of the receive buffer (before the process
         group is destroyed)."""
-        for name in ("_peer_recv", "_handle"):
+        for name in ("_graph", "_peer_recv", "_handle"):
             if hasattr(self, name):
                 delattr(self, name)
 

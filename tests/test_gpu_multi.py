@@ -22,7 +22,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, transport, buckets, q):
+def _worker(rank, world, port, transport, buckets, q, graph=False):
     try:
         import datetime
         import sys
@@ -40,8 +40,14 @@ def _worker(rank, world, port, transport, buckets, q):
         banks = [torch.randn(*s, generator=g).to(dev) for s in SHAPES]
         step = ShardedOrthogonalizer(SHAPES, method="PS2_55", device=dev, transport=transport,
                                      buckets=buckets)
-        for _ in range(2):  # a second step reuses the buffers behind the barriers
-            step(banks)
+        if graph:
+            step.capture(banks)
+            for _ in range(2):
+                step.replay()
+        else:
+            for _ in range(2):  # a second step reuses the buffers behind the barriers
+                step(banks)
+        torch.cuda.synchronize()
         got = [t.cpu() for t in step.gathered_banks()]
         polar = make_polynomial_orthogonalizer("PS2_55")
         want = [polar(b).half().cpu() for b in banks]
@@ -54,15 +60,15 @@ def _worker(rank, world, port, transport, buckets, q):
         q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
 
 
-@pytest.mark.parametrize("transport,buckets", [("copy_engine", None), ("copy_engine", 3),
-                                               ("collective", 2)])
-def test_two_gpu_step_matches_single_process(cuda_device, transport, buckets):
+@pytest.mark.parametrize("transport,buckets,graph", [("copy_engine", None, False), ("copy_engine", 3, False),
+                                                     ("collective", 2, False), ("copy_engine", 2, True)])
+def test_two_gpu_step_matches_single_process(cuda_device, transport, buckets, graph):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, buckets, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, buckets, q, graph)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
