@@ -350,8 +350,8 @@ def main():
                          "gather/compute overlap (default: auto)")
     ap.add_argument("--gemm-ctas", type=int, default=None,
                     help="multi-GPU: cap on GEMM CTAs, leaving SMs to the all-gather")
-    ap.add_argument("--graph", action="store_true",
-                    help="capture the step as a CUDA graph once and replay it in the timed region")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="enqueue every step from the host instead of replaying a CUDA graph of it")
     ap.add_argument("--transport", default="auto", choices=["auto", "copy_engine", "collective"],
                     help="multi-GPU: copy-engine pushes into symmetric memory, or the NCCL all-gather")
     ap.add_argument("--sweep", action="store_true",
@@ -507,9 +507,9 @@ def main():
             "gpu_launches": launches,
             "host_enqueue_ms_per_step": host_ms,
         }
+        line["config"]["cuda_graph"] = bool(args.graph)
         if world > 1:
             line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
-                                        "cuda_graph": bool(args.graph),
                                         "gemm_ctas": args.gemm_ctas,
                                         "bucket_matrices": [sum(c for _, _, c in p["pieces"]) for p in step.plans],
                                         "bytes_per_step": step.recv.numel() * 2}
