@@ -433,20 +433,23 @@ def main():
     prof = nat.profile_read()
     nat.profile_enable(False)
 
-    # End-to-end through the public API with host buffers: each rank uploads
-    # its own slices from pinned memory, runs the step, and downloads the full
-    # gathered FP16 update set.
+    # End-to-end through the public API with host buffers (step_host): each
+    # rank uploads its own slices from pinned memory bucket by bucket, computes
+    # each bucket as its inputs land and downloads the full gathered FP16
+    # update set, the transfers overlapping the circuits. With one GPU the
+    # host path uses its own plan of 8 buckets (the device-resident step above
+    # needs none).
     host_banks = [b.cpu().pin_memory() for b in banks]
-    host_out = torch.empty(step.recv.numel(), dtype=torch.float16).pin_memory()
-    ranges = step.local_ranges()
+    host_step = step
+    if world == 1:
+        host_step = ShardedOrthogonalizer(shapes, method=method, group=None, device=device,
+                                          world_size=1, rank=0, buckets=8)
+    host_out = torch.empty(host_step.recv.numel(), dtype=torch.float16).pin_memory()
+    ranges = host_step.local_ranges()
     h2d = sum(count * shapes[g][1] * shapes[g][2] * 4 for g, _, count in ranges)
-    dev_banks = [torch.empty_like(b) for b in banks]
 
     def e2e_step():
-        for g, start, count in ranges:
-            dev_banks[g][start:start + count].copy_(host_banks[g][start:start + count], non_blocking=True)
-        out = step(dev_banks)
-        host_out.copy_(out, non_blocking=True)
+        host_step.step_host(host_banks, host_out)
 
     e2e_step()
     barrier()
@@ -458,6 +461,8 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.e2e_steps, world, device)
     d2h = host_out.numel() * 2
+    if host_step is not step:
+        host_step.close()
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

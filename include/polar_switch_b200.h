@@ -91,7 +91,7 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
 
 /* Selects the GEMM kernel for later launches: 0 = one-CTA kernel (128 x 256
  * tiles), 1 = CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles over two
- * SMs), 2 (default) = CTA pairs for squares of buffers with n <= 2048, the
+ * SMs), 2 (default) = CTA pairs for squares of buffers with n <= 1024, the
  * one-CTA kernel for everything else. All compute the same products with the
  * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);

@@ -56,7 +56,7 @@ long long g_wait_limit = ps::kDefaultWaitLimit;
 // one-CTA kernel for everything else (Grams, applies and large squares run
 // faster there).
 int g_pair_mode = 2;
-constexpr int64_t kPairMaxN = 2048;
+constexpr int64_t kPairMaxN = 1024;
 // Upper bound on the CTAs (SMs) a persistent GEMM grid may take; 0 = all SMs.
 // Leaving SMs free lets a collective run beside the GEMMs.
 int g_max_ctas = 0;

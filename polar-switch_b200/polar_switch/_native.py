@@ -174,7 +174,7 @@ def profile_read():
 
 def set_cta_pairs(mode):
     """GEMM kernel selection: 0/False one-CTA kernel, 1/True CTA pairs, 2 (default) CTA
-    pairs for squares with n <= 2048 only. Returns the previous mode (an int)."""
+    pairs for squares with n <= 1024 only. Returns the previous mode (an int)."""
     rc = load().ps_set_cta_pairs(int(mode))
     if rc < 0:
         check("ps_set_cta_pairs", rc)

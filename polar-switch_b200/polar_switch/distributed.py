@@ -271,6 +271,9 @@ class ShardedOrthogonalizer:
                 raise ValueError(f"bank shape {tuple(X.shape)} does not match the plan {shape}")
 
     def _compute_bucket(self, banks, plan):
+        ready = getattr(self, "_input_events", None)
+        if ready is not None:  # inputs of this bucket still arriving from the host
+            torch.cuda.current_stream(self.device).wait_event(ready[id(plan)])
         inputs, outputs = [], []
         for g, start, view in self._segment_views(plan, self.rank):
             inputs.append(banks[g][start:start + view.shape[0]])
@@ -346,6 +349,56 @@ class ShardedOrthogonalizer:
         self._barrier_on(comm)
         main.wait_stream(comm)
 
+    def step_host(self, host_banks, host_out=None):
+        """One step from host memory: copies this rank's slices of `host_banks`
+        (pinned CPU tensors shaped like the plan) to the device bucket by bucket
+        on a copy stream, computes each bucket as soon as its inputs are there,
+        and copies the gathered FP16 result back into `host_out` (a pinned FP16
+        tensor of `recv`'s size; allocated when None) -- with one rank bucket by
+        bucket as each finishes, with several once the exchange is complete.
+        Transfers in both directions overlap the circuits. Returns `host_out`,
+        valid once the caller's current stream has reached this point."""
+        if self.device.type != "cuda":
+            raise ValueError("step_host needs a CUDA device")
+        self._check(host_banks)
+        dev = self.device
+        if getattr(self, "_dev_in", None) is None:
+            self._dev_in = [torch.empty(b.shape, dtype=b.dtype, device=dev) for b in host_banks]
+            self._h2d = torch.cuda.Stream(device=dev)
+            self._d2h = torch.cuda.Stream(device=dev)
+        if host_out is None:
+            host_out = torch.empty(self.recv.numel(), dtype=torch.float16, pin_memory=True)
+        main = torch.cuda.current_stream(dev)
+        self._h2d.wait_stream(main)  # the staging buffers are free again
+        events = {}
+        with torch.cuda.stream(self._h2d):
+            for plan in self.plans:
+                for g, start, view in self._segment_views(plan, self.rank):
+                    n = view.shape[0]
+                    self._dev_in[g][start:start + n].copy_(host_banks[g][start:start + n], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self._h2d)
+                events[id(plan)] = ev
+        self._input_events = events
+        try:
+            if self.world_size == 1:
+                for plan in self.plans:
+                    self._compute_bucket(self._dev_in, plan)
+                    self._d2h.wait_stream(main)
+                    region = self._region(plan)
+                    with torch.cuda.stream(self._d2h):
+                        host_out[plan["offset"]:plan["offset"] + region.numel()].copy_(region, non_blocking=True)
+            else:
+                self(self._dev_in)
+                self._d2h.wait_stream(main)
+                with torch.cuda.stream(self._d2h):
+                    host_out.copy_(self.recv, non_blocking=True)
+        finally:
+            self._input_events = None
+        main.wait_stream(self._d2h)
+        main.wait_stream(self._h2d)
+        return host_out
+
     def capture(self, banks, warmup=2):
         """Record one whole step on these bank tensors as a CUDA graph (after
         `warmup` eager steps); `replay()` then runs it again with no host work
@@ -371,7 +424,7 @@ class ShardedOrthogonalizer:
     def close(self):
         """Drop the peer mappings of the receive buffer (before the process
         group is destroyed)."""
-        for name in ("_graph", "_peer_recv", "_handle"):
+        for name in ("_graph", "_peer_recv", "_handle", "_dev_in"):
             if hasattr(self, name):
                 delattr(self, name)
 

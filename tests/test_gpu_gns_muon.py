@@ -123,6 +123,28 @@ def test_sharded_step_cuda_graph_replay(cuda_device):
     step.close()
 
 
+def test_sharded_step_from_host_memory(cuda_device):
+    """step_host: pinned host banks in, pinned FP16 results out, bucket by
+    bucket with overlapped copies; equal to the device-resident step."""
+    from polar_switch.distributed import ShardedOrthogonalizer
+    shapes = [(3, 256, 128), (4, 128, 128), (2, 128, 384), (5, 264, 128)]
+    host = [seeded(s, 80 + i).pin_memory() for i, s in enumerate(shapes)]
+    step = ShardedOrthogonalizer(shapes, method="PS2_55", device=cuda_device, world_size=1, rank=0,
+                                 buckets=3)
+    out = step.step_host(host)
+    torch.cuda.synchronize()
+    got = out.clone()
+    out2 = step.step_host(host, out)  # second call reuses the staging and the output buffer
+    torch.cuda.synchronize()
+    assert out2.data_ptr() == out.data_ptr() and torch.equal(out2, got)
+    ref = ShardedOrthogonalizer(shapes, method="PS2_55", device=cuda_device, world_size=1, rank=0,
+                                buckets=3)
+    ref([h.to(cuda_device) for h in host])
+    assert torch.equal(got, ref.recv.cpu())
+    step.close()
+    ref.close()
+
+
 def test_status_word_and_bounded_wait(cuda_device):
     """A kernel whose wait can never complete gives up after its limit and
     records status 5; the context stays usable afterwards."""

@@ -40,7 +40,11 @@ def _worker(rank, world, port, transport, buckets, q, graph=False):
         banks = [torch.randn(*s, generator=g).to(dev) for s in SHAPES]
         step = ShardedOrthogonalizer(SHAPES, method="PS2_55", device=dev, transport=transport,
                                      buckets=buckets)
-        if graph:
+        if graph == "host":
+            out = step.step_host([b.cpu().pin_memory() for b in banks])
+            torch.cuda.synchronize()
+            step.recv.copy_(out.to(dev))
+        elif graph:
             step.capture(banks)
             for _ in range(2):
                 step.replay()
@@ -61,7 +65,8 @@ def _worker(rank, world, port, transport, buckets, q, graph=False):
 
 
 @pytest.mark.parametrize("transport,buckets,graph", [("copy_engine", None, False), ("copy_engine", 3, False),
-                                                     ("collective", 2, False), ("copy_engine", 2, True)])
+                                                     ("collective", 2, False), ("copy_engine", 2, True),
+                                                     ("copy_engine", 2, "host")])
 def test_two_gpu_step_matches_single_process(cuda_device, transport, buckets, graph):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

@@ -46,3 +46,18 @@ def test_struct_layouts_match_header():
     # ps_step: 3 x int32 + 3 x float; ps_problem: pointers and int64 fields
     assert ctypes.sizeof(_native.PsStep) == 24
     assert ctypes.sizeof(_native.PsProblem) == 8 + 8 + 6 * 8 + 8 + 8
+
+
+def test_host_side_knobs_round_trip_without_gpu():
+    """Kernel-selection and scheduling knobs are host state: they validate their
+    argument and return the previous setting, with no device present."""
+    lib = _native.load()
+    assert lib.ps_set_cta_pairs(3) == _native.PS_ERR_INVALID
+    assert lib.ps_set_cta_pairs(-1) == _native.PS_ERR_INVALID
+    prev = lib.ps_set_cta_pairs(1)
+    assert prev == 2  # default: pairs for small squares only
+    assert lib.ps_set_cta_pairs(0) == 1
+    assert lib.ps_set_cta_pairs(prev) == 0
+    assert lib.ps_set_max_ctas(-5) == _native.PS_ERR_INVALID
+    assert lib.ps_set_max_ctas(100) == 0
+    assert lib.ps_set_max_ctas(0) == 100
