@@ -177,6 +177,13 @@ def run_reference(args, world, rank):
     from polar_switch import circuit_flops, coefficients
     table = getattr(coefficients, method)
     flops = sum(L * circuit_flops(table, r, c) for L, r, c in shapes)
+    # torchrun sets OMP_NUM_THREADS=1 per rank; rank 0 runs alone here and
+    # takes every core it may run on.
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    torch.set_num_threads(max(cores, 1))
     threads = torch.get_num_threads()
     times = []
     for i in range(args.warmup + args.steps):
