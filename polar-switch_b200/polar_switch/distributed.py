@@ -10,14 +10,20 @@ training/train_nanogpt.py:3983-4037, 4119-4218). Here
     on the per-matrix circuit FLOPs so every rank gets about the same work;
     the plan is a pure function of the shapes, so every rank computes the same
     plan without communication;
-  * `plan_buckets` cuts the matrices into a few consecutive buckets of about
-    equal cost, so communication of one bucket overlaps the next one's math;
+  * `plan_buckets` cuts the matrices into a few consecutive buckets of chosen
+    cost fractions (`auto_bucket_fractions`), so the transfer of one bucket
+    overlaps the next one's math;
   * `ShardedOrthogonalizer` runs each bucket's local slices as one grouped
-    circuit whose FP16 results land directly in that bucket's packed send
-    segment (the circuit rounds to FP16, so FP16 is lossless), then an
-    asynchronous in-place NCCL all_gather_into_tensor of the bucket gives every
-    rank its updates while the next bucket computes. With one rank nothing is
-    communicated.
+    circuit whose FP16 results land directly in that bucket's packed segment
+    of the receive buffer (the circuit rounds to FP16, so FP16 is lossless).
+    Each finished segment then reaches the other ranks while the next bucket
+    computes: by default every rank pushes it into every peer's receive
+    buffer (symmetric memory) with peer-to-peer copies that run on the copy
+    engines, leaving the SMs to the circuits; alternatively an asynchronous
+    in-place all_gather_into_tensor of the group's backend. With one rank
+    nothing is communicated. `step_host` runs a step from and to pinned host
+    memory with the transfers overlapping the circuits; `capture` / `replay`
+    record a step as a CUDA graph.
 """
 
 import heapq
