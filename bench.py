@@ -274,17 +274,17 @@ def run_kernel(args):
 PUBLISHED_MS = {
     (1, 8192, 8192): {"PS2_55": 7.47, "PS3_55": 7.47},
     (1, 16384, 16384): {"PS2_55": 55.7, "PS3_55": 56.0},
-    (1, 14336, 4096): {"PS2_55": 1.87, "PS3_55": 1.86},
-    (1, 28672, 8192): {"PS2_55": 13.9, "PS3_55": 14.0},
-    (1, 53248, 16384): {"PS2_55": 102.0, "PS3_55": 103.0},
-    (1, 4096, 14336): {"PS2_55": 1.86, "PS3_55": 1.88},
-    (1, 8192, 28672): {"PS2_55": 13.9, "PS3_55": 13.9},
-    (1, 16384, 53248): {"PS2_55": 102.0, "PS3_55": 103.0},
+    (1, 14336, 4096): {"PS2_55": 1.87, "PS3_55": 1.86, "GNS": 2.24},
+    (1, 28672, 8192): {"PS2_55": 13.9, "PS3_55": 14.0, "GNS": 16.3},
+    (1, 53248, 16384): {"PS2_55": 102.0, "PS3_55": 103.0, "GNS": 120.0},
+    (1, 4096, 14336): {"PS2_55": 1.86, "PS3_55": 1.88, "GNS": 2.25},
+    (1, 8192, 28672): {"PS2_55": 13.9, "PS3_55": 13.9, "GNS": 16.3},
+    (1, 16384, 53248): {"PS2_55": 102.0, "PS3_55": 103.0, "GNS": 119.0},
     (64, 4096, 4096): {"PS2_55": 59.8, "PS3_55": 59.4},
-    (216, 7168, 2048): {"PS2_55": 55.7, "PS3_55": 55.0},
-    (128, 8192, 1024): {"PS2_55": 9.70, "PS3_55": 9.42},
-    (216, 2048, 7168): {"PS2_55": 55.9, "PS3_55": 54.1},
-    (128, 1024, 8192): {"PS2_55": 9.72, "PS3_55": 9.34},
+    (216, 7168, 2048): {"PS2_55": 55.7, "PS3_55": 55.0, "GNS": 65.9},
+    (128, 8192, 1024): {"PS2_55": 9.70, "PS3_55": 9.42, "GNS": 10.9},
+    (216, 2048, 7168): {"PS2_55": 55.9, "PS3_55": 54.1, "GNS": 65.6},
+    (128, 1024, 8192): {"PS2_55": 9.72, "PS3_55": 9.34, "GNS": 10.8},
 }
 
 
@@ -306,9 +306,13 @@ def run_sweep(args):
     peak = peaks.get("bf16_tflops", 1590.0)
     for shape, pub in PUBLISHED_MS.items():
         X = torch.randn(shape, generator=g, device=device, dtype=torch.float16)
-        for method in ("PS2_55", "PS3_55"):
+        for method in [m for m in ("PS2_55", "PS3_55", "GNS") if m in pub and m in args.methods]:
             polar = make_polynomial_orthogonalizer(method)
-            flops = shape[0] * circuit_flops(getattr(coefficients, method), shape[1], shape[2])
+            if method == "GNS":  # the reference's count for GNS: (6a + 14) n^3
+                n, m = min(shape[1:]), max(shape[1:])
+                flops = shape[0] * (6 * m / n + 14) * n ** 3
+            else:
+                flops = shape[0] * circuit_flops(getattr(coefficients, method), shape[1], shape[2])
             # Warm up by time as well as by count: clocks take a while to settle
             # after the previous (possibly power-capped) shape.
             t_end = time.time() + 0.5
@@ -363,6 +367,7 @@ def main():
                     help="multi-GPU: copy-engine pushes into symmetric memory, or the NCCL all-gather")
     ap.add_argument("--sweep", action="store_true",
                     help="median circuit latency on every shape with a published reference latency")
+    ap.add_argument("--methods", default="PS2_55,PS3_55,GNS", help="--sweep: methods to time")
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
