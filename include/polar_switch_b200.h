@@ -96,7 +96,24 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
  * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);
 
-/* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
+/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
+PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
+
+/* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch
+ * of polar_switch/gram_newton_schulz.py:75-122): normalise, R = X X^T (X^T X
+ * when rows > cols), then for iteration i with coeffs[3i..3i+2] = (a, b, c):
+ * Z = c R R + b R; Q = Z + a I at i = 0 and at restarts, else Q = Q Z + a Q;
+ * before the next iteration (unless it restarts) R = Z (R Z + a R) + a (R Z
+ * + a R); iteration i in `resets` (i > 0) first sets X <- Q X and R from it.
+ * y = Q X (X Q when tall). Every product is one tcgen05 launch with FP32
+ * accumulation and one FP16 rounding. Square matrices are rejected
+ * (PS_ERR_INVALID): the reference sends them to Polar Express. */
+PS_API int ps_gns(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                  int64_t sR, int64_t sC, void* y, int y_dtype, int n_iter, const float* coeffs,
+                  int n_resets, const int32_t* resets, float eps, void* workspace,
+                  int64_t workspace_bytes, void* stream);
+
+/* Caps the number of CTAs/* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
  * afterwards; 0 (default) = every SM. Leaving SMs free lets a collective on
  * another stream run beside the GEMMs. Returns the previous cap. */
 PS_API int ps_set_max_ctas(int max_ctas);

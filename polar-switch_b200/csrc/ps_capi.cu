@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/polar_switch_b200.h"
@@ -656,6 +657,21 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
   }
 }
 
+int add_diag_impl(const void* in, void* out, int64_t L, int64_t n, float a, cudaStream_t stream) {
+  if (!in || !out) return fail(PS_ERR_INVALID, "ps_add_diag: null pointer");
+  if (!dims_ok(L, n, n)) return fail(PS_ERR_INVALID, "ps_add_diag: bad sizes");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int64_t blocks = (L * n * n + ps::NORM_THREADS - 1) / ps::NORM_THREADS;
+  if (blocks > 8LL * st->sms) blocks = 8LL * st->sms;
+  LaunchScope scope(kProfOther, stream, 0.0, 4.0 * L * n * n);
+  ps::ps_add_diag_kernel<<<static_cast<unsigned>(blocks), ps::NORM_THREADS, 0, stream>>>(
+      static_cast<const __half*>(in), static_cast<__half*>(out), L, n, a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "add_diag launch");
+}
+
 // ------------------------------------------------------------------ normalise
 int norm_chunks(int64_t L, int64_t rows, int64_t cols, int sms) {
   // Enough blocks in flight for HBM bandwidth: about 4 per SM in total.
@@ -1023,19 +1039,7 @@ int ps_apply(const void* b, const void* x, void* y, int64_t L, int64_t rows, int
 }
 
 int ps_add_diag(const void* in, void* out, int64_t L, int64_t n, float a, void* stream) {
-  if (!in || !out) return fail(PS_ERR_INVALID, "ps_add_diag: null pointer");
-  if (!dims_ok(L, n, n)) return fail(PS_ERR_INVALID, "ps_add_diag: bad sizes");
-  DeviceState* st = nullptr;
-  int rc = device_state(&st);
-  if (rc) return rc;
-  int64_t blocks = (L * n * n + ps::NORM_THREADS - 1) / ps::NORM_THREADS;
-  if (blocks > 8LL * st->sms) blocks = 8LL * st->sms;
-  LaunchScope scope(kProfOther, static_cast<cudaStream_t>(stream), 0.0, 4.0 * L * n * n);
-  ps::ps_add_diag_kernel<<<static_cast<unsigned>(blocks), ps::NORM_THREADS, 0,
-                           static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(in), static_cast<__half*>(out), L, n, a);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? PS_OK : cuda_fail(e, "add_diag launch");
+  return add_diag_impl(in, out, L, n, a, static_cast<cudaStream_t>(stream));
 }
 
 int64_t ps_circuit_workspace_bytes(int64_t L, int64_t rows, int64_t cols, int buffers) {
@@ -1169,6 +1173,103 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
       return rc;
   }
   return PS_OK;
+}
+
+// ---------------------------------------------------------------- Gram Newton-Schulz
+// The recurrence of polar_switch/gram_newton_schulz.py:75-122 as one C call:
+// R = X X^T (X^T X for tall X) once, per iteration Z = c R R + b R, Q = Z + a I
+// after a (re)start else Q = Q Z + a Q, and between restarts R = Z (R Z + a R)
+// + a (R Z + a R); at a restart X <- Q X and R is formed again; finally
+// X <- Q X. The buffers are stored in full (mirrored): a product of two
+// different matrices is symmetric only up to rounding, so unlike a square its
+// diagonal blocks are not bit-symmetric and could not be read back transposed
+// exactly; full storage keeps every step identical to the op-by-op recurrence.
+constexpr int kGnsBuffers = 5;
+
+int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols) {
+  if (!dims_ok(L, rows, cols)) return fail(PS_ERR_INVALID, "ps_gns: bad sizes");
+  DeviceState* st = nullptr;
+  if (device_state(&st)) return -1;
+  return circuit_layout(L, rows, cols, kGnsBuffers, st->sms).total;
+}
+
+int ps_gns(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+           int64_t sR, int64_t sC, void* y, int y_dtype, int n_iter, const float* coeffs,
+           int n_resets, const int32_t* resets, float eps, void* workspace, int64_t workspace_bytes,
+           void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!x || !y || !workspace || !coeffs || (n_resets > 0 && !resets))
+    return fail(PS_ERR_INVALID, "ps_gns: null pointer");
+  if (!dims_ok(L, rows, cols)) return fail(PS_ERR_INVALID, "ps_gns: bad sizes");
+  if (rows == cols)
+    return fail(PS_ERR_INVALID, "ps_gns: square matrices take Polar Express, not the Gram recurrence");
+  if (n_iter < 1 || n_iter > 64 || n_resets < 0 || n_resets > 64)
+    return fail(PS_ERR_INVALID, "ps_gns: bad iteration or restart count");
+  for (int i = 0; i < 3 * n_iter; ++i)
+    if (!std::isfinite(coeffs[i])) return fail(PS_ERR_INVALID, "ps_gns: non-finite coefficient");
+  if (elem_bytes(x_dtype) == 0 || elem_bytes(y_dtype) == 0)
+    return fail(PS_ERR_INVALID, "ps_gns: bad dtype");
+  if (!aligned16(workspace)) return fail(PS_ERR_INVALID, "ps_gns: workspace misaligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const CircuitLayout lay = circuit_layout(L, rows, cols, kGnsBuffers, st->sms);
+  if (workspace_bytes < lay.total) return fail(PS_ERR_WORKSPACE, "ps_gns: workspace too small");
+  auto is_reset = [&](int i) {
+    for (int k = 0; k < n_resets; ++k)
+      if (resets[k] == i) return true;
+    return false;
+  };
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* xh[2] = {ws, ws + lay.xh_bytes};
+  auto buf = [&](int k) -> void* { return ws + 2 * lay.xh_bytes + k * lay.buf_bytes; };
+  uint8_t* norm = ws + 2 * lay.xh_bytes + kGnsBuffers * lay.buf_bytes;
+  const int64_t Rp = lay.Rp, Cp = lay.Cp, n = lay.n;
+  const bool tall = lay.tall, tri = false;
+  int R = 0, Z = 1, Q = 2, Q2 = 3, RZ = 4, cur = 0;
+  if ((rc = normalize_impl(x, x_dtype, L, rows, cols, sL, sR, sC, eps, xh[0], Rp, Cp, norm,
+                           lay.norm_bytes, s)))
+    return rc;
+  if ((rc = gram_impl(xh[cur], buf(R), L, Rp, Cp, Cp, tall, s, tri))) return rc;
+  const int last = n_iter - 1;
+  for (int i = 0; i < n_iter; ++i) {
+    const float a = coeffs[3 * i], b = coeffs[3 * i + 1], c = coeffs[3 * i + 2];
+    const bool restart = i != 0 && is_reset(i);
+    if (restart) {
+      if ((rc = apply_impl(buf(Q), xh[cur], xh[1 - cur], L, Rp, Cp, Cp, 0.f, PS_F16, Cp, tall, s,
+                           tri)))
+        return rc;
+      cur = 1 - cur;
+      if ((rc = gram_impl(xh[cur], buf(R), L, Rp, Cp, Cp, tall, s, tri))) return rc;
+    }
+    if ((rc = sym_product_impl(buf(R), buf(R), buf(R), buf(Z), L, n, c, b, 0.f, s, "ps_gns", tri)))
+      return rc;
+    if (i == 0 || is_reset(i)) {
+      if ((rc = add_diag_impl(buf(Z), buf(Q), L, n, a, s))) return rc;
+    } else {
+      if ((rc = sym_product_impl(buf(Q), buf(Z), buf(Q), buf(Q2), L, n, 1.f, a, 0.f, s, "ps_gns",
+                                 tri)))
+        return rc;
+      std::swap(Q, Q2);
+    }
+    if (i < last && !is_reset(i + 1)) {
+      if ((rc = sym_product_impl(buf(R), buf(Z), buf(R), buf(RZ), L, n, 1.f, a, 0.f, s, "ps_gns",
+                                 tri)))
+        return rc;
+      if ((rc = sym_product_impl(buf(Z), buf(RZ), buf(RZ), buf(R), L, n, 1.f, a, 0.f, s, "ps_gns",
+                                 tri)))
+        return rc;
+    }
+  }
+  // X <- Q X, straight into y when its layout allows TMA stores.
+  const bool direct = (y_dtype == PS_F16 || y_dtype == PS_F32 || y_dtype == PS_BF16) &&
+                      Rp == rows && Cp == cols && (cols * elem_bytes(y_dtype)) % 16 == 0 &&
+                      aligned16(y);
+  if (direct)
+    return apply_impl(buf(Q), xh[cur], y, L, Rp, Cp, Cp, 0.f, y_dtype, cols, tall, s, tri);
+  if ((rc = apply_impl(buf(Q), xh[cur], xh[1 - cur], L, Rp, Cp, Cp, 0.f, PS_F16, Cp, tall, s, tri)))
+    return rc;
+  return copy_out(xh[1 - cur], Rp, Cp, rows, cols, L, y, y_dtype, st->sms, s);
 }
 
 // ---------------------------------------------------------------- no-alloc normalise

@@ -29,7 +29,7 @@ EXPORTED = (
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
     "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs",
-    "ps_set_max_ctas",
+    "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns",
 )
 
 
@@ -85,6 +85,9 @@ _SIGNATURES = {
     "ps_launch_count": ([], ctypes.c_longlong),
     "ps_set_cta_pairs": ([_int], _int),
     "ps_set_max_ctas": ([_int], _int),
+    "ps_gns_workspace_bytes": ([_i64, _i64, _i64], _i64),
+    "ps_gns": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _int, _int, ctypes.POINTER(_f32),
+                _int, ctypes.POINTER(ctypes.c_int32), _f32, _ptr, _i64, _ptr], _int),
     "ps_profile_enable": ([_int], _int),
     "ps_profile_read": ([_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i64),
                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)], _int),

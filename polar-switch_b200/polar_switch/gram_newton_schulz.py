@@ -51,7 +51,42 @@ def gns_flops(rows, cols, batch=1):
 
 def gram_newton_schulz(X, coefficients=GNS_COEFFICIENTS, reset_iterations=RESET_ITERATIONS,
                        epsilon=1e-7):
-    """Run the GNS recurrence on CUDA X (..., rows, cols); returns X's dtype and shape."""
+    """Run the GNS recurrence on CUDA X (..., rows, cols) as one library call
+    (ps_gns: workspace, padding of dimensions that are not multiples of 8 and
+    the output cast all inside it); returns X's dtype and shape."""
+    import ctypes
+
+    from . import _native as nat
+    if not isinstance(X, torch.Tensor) or not X.is_cuda:
+        raise NotImplementedError("gram_newton_schulz: polar_switch_b200 runs on CUDA tensors only")
+    shape, dtype = X.shape, X.dtype
+    if dtype not in nat.DTYPE_CODES:
+        raise TypeError(f"Unsupported dtype {dtype}")
+    W = X.reshape(-1, *shape[-2:])
+    L, rows, cols = W.shape
+    Y = torch.empty(W.shape, device=X.device, dtype=dtype)
+    flat = [float(v) for abc in coefficients for v in abc]
+    coeffs = (ctypes.c_float * len(flat))(*flat)
+    resets = (ctypes.c_int32 * max(len(reset_iterations), 1))(*reset_iterations)
+    lib = nat.load()
+    with torch.cuda.device(X.device):
+        ws_bytes = lib.ps_gns_workspace_bytes(L, rows, cols)
+        if ws_bytes < 0:
+            nat.check("ps_gns_workspace_bytes", ws_bytes)
+        ws = torch.empty(ws_bytes, device=X.device, dtype=torch.uint8)
+        sL, sR, sC = W.stride()
+        nat.check("ps_gns", lib.ps_gns(
+            nat.ptr(W), nat.DTYPE_CODES[dtype], L, rows, cols, sL, sR, sC, nat.ptr(Y),
+            nat.DTYPE_CODES[dtype], len(coefficients), coeffs, len(reset_iterations), resets,
+            float(epsilon), nat.ptr(ws), ws_bytes, nat.stream_ptr(X.device)))
+    return Y.reshape(shape)
+
+
+def gram_newton_schulz_ops(X, coefficients=GNS_COEFFICIENTS, reset_iterations=RESET_ITERATIONS,
+                           epsilon=1e-7):
+    """The same recurrence op by op through the public kernels (full, mirrored
+    n x n buffers); kept as the step-by-step form of `gram_newton_schulz`,
+    which must give the same bits."""
     shape, dtype = X.shape, X.dtype
     Xh = cuda_ops.normalize(X.reshape(-1, *shape[-2:]), epsilon)
     tall = Xh.shape[-2] > Xh.shape[-1]

@@ -34,6 +34,29 @@ def test_gns_rectangular(cuda_device, shape):
     assert 0.787 - 2e-3 <= lo and hi <= 1.213 + 2e-3
 
 
+@pytest.mark.parametrize("shape", [(2, 256, 768), (3, 384, 128), (1, 1024, 2048), (2, 136, 200),
+                                   (1, 2048, 512)])
+def test_gns_one_call_matches_op_by_op(cuda_device, shape):
+    """ps_gns runs the whole recurrence in one call; the result equals the
+    op-by-op recurrence through the public kernels bit for bit."""
+    from polar_switch.gram_newton_schulz import gram_newton_schulz, gram_newton_schulz_ops
+    X = seeded(shape, 90).to(cuda_device)
+    assert torch.equal(gram_newton_schulz(X), gram_newton_schulz_ops(X))
+
+
+def test_gns_padded_shape_against_oracle(cuda_device):
+    """Dimensions that are not multiples of 8 are zero-padded inside ps_gns."""
+    from polar_switch import make_polynomial_orthogonalizer
+    from polar_switch.gram_newton_schulz import GNS_COEFFICIENTS
+    X = seeded((2, 130, 66), 91)
+    got = make_polynomial_orthogonalizer("GNS")(X.to(cuda_device)).cpu()
+    ref64 = og.gns_run(X, GNS_COEFFICIENTS, acc=torch.float64)
+    ref32 = og.gns_run(X, GNS_COEFFICIENTS, acc=torch.float32)
+    err = oc.relative_frobenius(got, ref64)
+    floor = oc.relative_frobenius(ref32, ref64)
+    assert err <= max(5e-3, 1.5 * floor), (err, floor)
+
+
 def test_gns_square_uses_polar_express(cuda_device):
     from polar_switch import make_polynomial_orthogonalizer
     X = seeded((192, 192), 31)
