@@ -63,9 +63,9 @@ def make_banks(shapes, device, seed=0, scale=1.0):
 # dominant kernel, from one ncu capture of each square kernel at the Qwen shape
 # (profiles/ps_gemm_square_qwen_n1024.md, one-CTA: 307.4 MB;
 # profiles/ps_gemm_pair_square_qwen_n1024.md, CTA pairs, the default for n = 1024:
-# 308.2 MB; each a launch over 64 matrices of n = 1024); scaled to a launch by
+# 309.0 MB; each a launch over 64 matrices of n = 1024); scaled to a launch by
 # its number of matrices.
-TRAFFIC_BYTES_PER_MATRIX = {("square", 1024): 308.2e6 / 64}
+TRAFFIC_BYTES_PER_MATRIX = {("square", 1024): 309.0e6 / 64}
 
 
 class ClockSampler:
