@@ -40,6 +40,17 @@ def test_invalid_arguments_are_rejected_before_any_device_work():
     assert lib.ps_gram(null, null, 1, 8, 8, 8, null) == _native.PS_ERR_INVALID
     assert b"null" in lib.ps_last_error()
     assert lib.ps_set_wait_limit(0) == _native.PS_ERR_INVALID
+    coeffs = (ctypes.c_float * 3)(1.0, 0.0, 0.0)
+    resets = (ctypes.c_int32 * 1)(0)
+    ws = ctypes.c_void_p(256)
+    # ps_gns: null pointers, a square shape and a bad iteration count are argument errors
+    assert lib.ps_gns(null, 1, 1, 8, 16, 128, 16, 1, null, 1, 1, coeffs, 0, resets, 1e-7, ws, 1 << 20,
+                      null) == _native.PS_ERR_INVALID
+    assert lib.ps_gns(ws, 1, 1, 16, 16, 256, 16, 1, ws, 1, 1, coeffs, 0, resets, 1e-7, ws, 1 << 20,
+                      null) == _native.PS_ERR_INVALID
+    assert b"square" in lib.ps_last_error()
+    assert lib.ps_gns(ws, 1, 1, 8, 16, 128, 16, 1, ws, 1, 0, coeffs, 0, resets, 1e-7, ws, 1 << 20,
+                      null) == _native.PS_ERR_INVALID
 
 
 def test_struct_layouts_match_header():
