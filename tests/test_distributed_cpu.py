@@ -174,3 +174,24 @@ def test_bucketed_layout_single_rank_views(buckets):
         for s, c in got:
             cover.extend(range(s, s + c))
         assert cover == list(range(L))
+
+
+def test_auto_buckets_follow_the_model():
+    """One rank needs no buckets; with more ranks the automatic fractions are
+    positive, and their modelled step is no slower than a single bucket."""
+    from polar_switch.distributed import (BUCKET_OVERHEAD_S, CIRCUIT_FLOPS_PER_S, GATHER_RECV_BYTES_PER_S,
+                                          auto_bucket_fractions, simulate_buckets)
+    banks = qwen3_0_6b_banks()
+    assert auto_bucket_fractions(banks, 1, flops) == 1
+    total = sum(L * flops(r, c) for L, r, c in banks)
+    elems = sum(L * r * c for L, r, c in banks)
+    for world in (2, 4, 8):
+        fr = auto_bucket_fractions(banks, world, flops)
+        fr = fr if isinstance(fr, list) else [1.0]
+        assert all(f > 0 for f in fr)
+        compute = total / world / CIRCUIT_FLOPS_PER_S
+        gather = (world - 1) / world * elems * 2 / GATHER_RECV_BYTES_PER_S
+        assert simulate_buckets(fr, compute, gather) <= simulate_buckets([1.0], compute, gather) + 1e-12
+        # a schedule never ends before its transfer, nor before its compute
+        t = simulate_buckets(fr, compute, gather)
+        assert t >= gather and t >= compute + BUCKET_OVERHEAD_S
