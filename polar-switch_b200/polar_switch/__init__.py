@@ -213,9 +213,20 @@ def make_polynomial_orthogonalizer(method, compile=True, epsilon=1e-7):
     circuit = _Circuit(table, buffers)
     events = []
 
+    from . import torch_ops
+    op_args = torch_ops.table_to_lists(table)
+
     def polar(X, out=None):
         """Approximate the polar factor of each matrix in X."""
         _check_input(X)
+        if torch.compiler.is_compiling():
+            # Traced by torch.compile: one polar_switch::circuit operator, no
+            # attribute updates (provenance is recorded by eager calls).
+            result = torch.ops.polar_switch.circuit(X, *op_args, buffers, float(epsilon))
+            if out is not None:
+                out.copy_(result)
+                result = out
+            return result
         result = circuit(X, epsilon, out=out)
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
@@ -236,3 +247,7 @@ def make_polynomial_orthogonalizer(method, compile=True, epsilon=1e-7):
     polar.buffers = buffers
     polar.epsilon = epsilon
     return polar
+
+
+# Registers the polar_switch:: operators used under torch.compile.
+from . import torch_ops  # noqa: E402,F401

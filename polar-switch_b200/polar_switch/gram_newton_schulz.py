@@ -136,13 +136,25 @@ def make_orthogonalizer(pe_factory, compile=True, epsilon=1e-7):
         raise ValueError("Use a positive finite epsilon")
     pe = pe_factory("POLAR_EXPRESS", compile=compile, epsilon=epsilon)
 
+    flat_coeffs = [float(v) for abc in GNS_COEFFICIENTS for v in abc]
+
     def polar(X, out=None):
         """Approximate the polar factor of each matrix in X."""
         _check_input(X)
+        compiling = torch.compiler.is_compiling()
         if X.shape[-2] == X.shape[-1]:
             result = pe(X, out=out)
-            polar.last_execution = dict(pe.last_execution, requested="GNS",
-                                        dispatch="square_polar_express")
+            if not compiling:
+                polar.last_execution = dict(pe.last_execution, requested="GNS",
+                                            dispatch="square_polar_express")
+            return result
+        if compiling:
+            # Traced by torch.compile: one polar_switch::gns operator, no
+            # attribute updates (provenance is recorded by eager calls).
+            result = torch.ops.polar_switch.gns(X, flat_coeffs, list(RESET_ITERATIONS), float(epsilon))
+            if out is not None:
+                out.copy_(result)
+                result = out
             return result
         result = gram_newton_schulz(X, epsilon=epsilon)
         if out is not None:
