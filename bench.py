@@ -36,6 +36,8 @@ WORKLOADS = {
     "nanogpt": dict(desc="Modded-NanoGPT Muon batch (BASELINE config 3)", method="PS3_55"),
     "single": dict(desc="single 8192x8192 matrix (BASELINE config 2, published heatmap point)",
                    method="PS2_55"),
+    "stress": dict(desc="stress batch 4 x 8192 x 28672 (BASELINE config 5); on more GPUs than "
+                        "matrices each matrix is split across ranks", method="PS3_55"),
 }
 
 
@@ -49,6 +51,8 @@ def bank_shapes(workload):
         return pd.nanogpt_banks()
     if workload == "single":
         return [(1, 8192, 8192)]
+    if workload == "stress":
+        return [(4, 8192, 28672)]
     raise ValueError(workload)
 
 
@@ -386,7 +390,7 @@ def main():
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     from polar_switch import _native as nat
-    from polar_switch.distributed import ShardedOrthogonalizer
+    from polar_switch.distributed import ShardedOrthogonalizer, make_sharded_orthogonalizer
 
     shapes = bank_shapes(args.workload)
     method = WORKLOADS[args.workload]["method"]
@@ -394,9 +398,9 @@ def main():
     buckets = args.buckets
     if buckets is not None:
         buckets = [float(f) for f in buckets.split(",")] if "," in buckets else int(buckets)
-    step = ShardedOrthogonalizer(shapes, method=method, group=None, device=device,
-                                 world_size=world, rank=rank, buckets=buckets,
-                                 gemm_ctas=args.gemm_ctas, transport=args.transport)
+    step = make_sharded_orthogonalizer(shapes, method=method, group=None, device=device,
+                                       world_size=world, rank=rank, buckets=buckets,
+                                       gemm_ctas=args.gemm_ctas, transport=args.transport)
     flops = step.flops_total
 
     def barrier():
@@ -527,6 +531,7 @@ def main():
         line["config"]["cuda_graph"] = bool(args.graph)
         if world > 1:
             line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
+                                        "split_matrices": type(step).__name__ == "SplitOrthogonalizer",
                                         "gemm_ctas": args.gemm_ctas,
                                         "bucket_matrices": [sum(c for _, _, c in p["pieces"]) for p in step.plans],
                                         "bytes_per_step": step.recv.numel() * 2}

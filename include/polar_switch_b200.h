@@ -96,7 +96,27 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
  * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);
 
-/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
+/* Pieces of the normalisation and of the Gram for a matrix split by columns
+ * (or, tall, by rows) across ranks, the split Muon step for banks with fewer
+ * matrices than ranks (no single counterpart in the reference; together they
+ * replace polar_switch/__init__.py:34-35 and the Gram of :41 when the partial
+ * results are summed across ranks between the calls):
+ *   ps_sumsq: sums[l] = sum of squares of x[l] (FP64, the same chunks and
+ *     order as ps_normalize); workspace of ps_normalize_workspace_bytes;
+ *   ps_scale_cast: xh[l] = fp16(x[l] / (sqrt(sums[l]) + eps)), padding zeroed;
+ *     sums == NULL gives a plain FP16 rounding (denominator 1);
+ *   ps_gram_f32: out[l] = X X^T (X^T X when rows > cols) in FP32, not rounded,
+ *     all n x n elements (general tiles). */
+PS_API int ps_sumsq(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                    int64_t sR, int64_t sC, double* sums, void* workspace, int64_t workspace_bytes,
+                    void* stream);
+PS_API int ps_scale_cast(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols,
+                         int64_t sL, int64_t sR, int64_t sC, const double* sums, float eps, void* xh,
+                         int64_t rows_p, int64_t cols_p, void* stream);
+PS_API int ps_gram_f32(const void* x, float* out, int64_t L, int64_t rows, int64_t cols,
+                       int64_t x_ld, void* stream);
+
+/* Scratch bytes ps_gns needs/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 
 /* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch

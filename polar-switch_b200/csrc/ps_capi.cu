@@ -700,39 +700,54 @@ int64_t norm_partials_per_matrix(int64_t L, int64_t rows, int64_t cols, int sms)
   return a > b ? a : b;
 }
 
-// Two passes. Contiguous input is summed over chunks of `chunk_elems`
-// elements, strided input over `chunks` row ranges.
+// Pass 1: chunk sums of squares. Contiguous input is summed over chunks of
+// `chunk_elems` elements, strided input over `chunks` row ranges; returns the
+// number of chunk sums per matrix through `chunks_out`.
 template <typename T>
-int launch_normalize(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL, int64_t sR,
-                     int64_t sC, float eps, void* xh, int64_t Rp, int64_t Cp, double* partial,
-                     int chunks, int64_t chunk_elems, int sms, cudaStream_t s) {
+int launch_norm_pass1(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL, int64_t sR,
+                      int64_t sC, double* partial, int chunks, int64_t chunk_elems, int* chunks_out,
+                      cudaStream_t s) {
   const int flat = (sC == 1 && sR == C) ? 1 : 0;
   if (flat) chunks = static_cast<int>((R * C + chunk_elems - 1) / chunk_elems);
+  *chunks_out = chunks;
   dim3 g1(chunks, static_cast<unsigned>(L));
-  const double in_bytes = static_cast<double>(L) * R * C * sizeof(T);
-  cudaError_t e;
-  {
-    LaunchScope scope(kProfNormalize, s, 2.0 * L * R * C, in_bytes);
-    ps::ps_norm_partial_kernel<T><<<g1, ps::NORM_THREADS, 0, s>>>(
-        static_cast<const T*>(x), R, C, sL, sR, sC, flat, chunks, chunk_elems, partial);
-    e = cudaGetLastError();
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 1)");
+  LaunchScope scope(kProfNormalize, s, 2.0 * L * R * C, static_cast<double>(L) * R * C * sizeof(T));
+  ps::ps_norm_partial_kernel<T><<<g1, ps::NORM_THREADS, 0, s>>>(
+      static_cast<const T*>(x), R, C, sL, sR, sC, flat, chunks, chunk_elems, partial);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "normalize launch (pass 1)");
+}
+
+// Pass 2: xh = fp16(x / den) with den from `chunks` sums per matrix (partial
+// == nullptr: den = 1, a plain FP16 rounding).
+template <typename T>
+int launch_norm_pass2(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL, int64_t sR,
+                      int64_t sC, const double* partial, int chunks, float eps, void* xh, int64_t Rp,
+                      int64_t Cp, int sms, cudaStream_t s) {
+  const int flat = (sC == 1 && sR == C) ? 1 : 0;
   const int64_t per_mat_blocks = (Rp * Cp + ps::NORM_THREADS * 8 - 1) / (ps::NORM_THREADS * 8);
   int64_t gx = (4LL * sms + L - 1) / L;
   if (gx > per_mat_blocks) gx = per_mat_blocks;
   if (gx < 1) gx = 1;
   dim3 g2(static_cast<unsigned>(gx), static_cast<unsigned>(L));
-  {
-    LaunchScope scope(kProfNormalize, s, static_cast<double>(L) * R * C,
-                      in_bytes + 2.0 * L * Rp * Cp);
-    ps::ps_scale_cast_kernel<T><<<g2, ps::NORM_THREADS, 0, s>>>(
-        static_cast<const T*>(x), R, C, sL, sR, sC, flat, partial, chunks, eps,
-        static_cast<__half*>(xh), Rp, Cp);
-    e = cudaGetLastError();
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 2)");
-  return PS_OK;
+  LaunchScope scope(kProfNormalize, s, static_cast<double>(L) * R * C,
+                    static_cast<double>(L) * R * C * sizeof(T) + 2.0 * L * Rp * Cp);
+  ps::ps_scale_cast_kernel<T><<<g2, ps::NORM_THREADS, 0, s>>>(
+      static_cast<const T*>(x), R, C, sL, sR, sC, flat, partial, chunks, eps,
+      static_cast<__half*>(xh), Rp, Cp);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "normalize launch (pass 2)");
+}
+
+// Two passes.
+template <typename T>
+int launch_normalize(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL, int64_t sR,
+                     int64_t sC, float eps, void* xh, int64_t Rp, int64_t Cp, double* partial,
+                     int chunks, int64_t chunk_elems, int sms, cudaStream_t s) {
+  int nch = 0;
+  int rc = launch_norm_pass1<T>(x, L, R, C, sL, sR, sC, partial, chunks, chunk_elems, &nch, s);
+  if (rc) return rc;
+  return launch_norm_pass2<T>(x, L, R, C, sL, sR, sC, partial, nch, eps, xh, Rp, Cp, sms, s);
 }
 
 int64_t normalize_ws_bytes(int64_t L, int64_t rows, int64_t cols, int sms) {
@@ -1013,6 +1028,103 @@ int ps_normalize(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t co
                  void* workspace, int64_t workspace_bytes, void* stream) {
   return normalize_impl(x, x_dtype, L, rows, cols, sL, sR, sC, eps, xh, rows_p, cols_p,
                         workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int ps_sumsq(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+             int64_t sR, int64_t sC, double* sums, void* workspace, int64_t workspace_bytes,
+             void* stream) {
+  if (!x || !sums || !workspace) return fail(PS_ERR_INVALID, "ps_sumsq: null pointer");
+  if (!dims_ok(L, rows, cols)) return fail(PS_ERR_INVALID, "ps_sumsq: bad sizes");
+  if (elem_bytes(x_dtype) == 0) return fail(PS_ERR_INVALID, "ps_sumsq: bad dtype");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  if (workspace_bytes < normalize_ws_bytes(L, rows, cols, st->sms))
+    return fail(PS_ERR_WORKSPACE, "ps_sumsq: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  double* partial = static_cast<double*>(workspace);
+  const int chunks = norm_chunks(L, rows, cols, st->sms);
+  const int64_t ce = ps::norm_chunk_elems(rows * cols);
+  int nch = 0;
+  switch (x_dtype) {
+    case PS_F16:
+      rc = launch_norm_pass1<__half>(x, L, rows, cols, sL, sR, sC, partial, chunks, ce, &nch, s);
+      break;
+    case PS_BF16:
+      rc = launch_norm_pass1<__nv_bfloat16>(x, L, rows, cols, sL, sR, sC, partial, chunks, ce, &nch, s);
+      break;
+    case PS_F32:
+      rc = launch_norm_pass1<float>(x, L, rows, cols, sL, sR, sC, partial, chunks, ce, &nch, s);
+      break;
+    default:
+      rc = launch_norm_pass1<double>(x, L, rows, cols, sL, sR, sC, partial, chunks, ce, &nch, s);
+  }
+  if (rc) return rc;
+  const int64_t blocks = (L + 7) / 8;
+  LaunchScope scope(kProfOther, s, 0.0, 8.0 * L * nch);
+  ps::ps_sum_partials_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(partial, nch, L, sums);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "sum-of-squares launch");
+}
+
+int ps_scale_cast(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                  int64_t sR, int64_t sC, const double* sums, float eps, void* xh, int64_t rows_p,
+                  int64_t cols_p, void* stream) {
+  if (!x || !xh) return fail(PS_ERR_INVALID, "ps_scale_cast: null pointer");
+  if (!dims_ok(L, rows, cols) || rows_p < rows || cols_p < cols)
+    return fail(PS_ERR_INVALID, "ps_scale_cast: bad sizes");
+  if (elem_bytes(x_dtype) == 0) return fail(PS_ERR_INVALID, "ps_scale_cast: bad dtype");
+  if (!std::isfinite(eps) || eps < 0.f)
+    return fail(PS_ERR_INVALID, "ps_scale_cast: eps must be finite and non-negative");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (x_dtype) {
+    case PS_F16:
+      return launch_norm_pass2<__half>(x, L, rows, cols, sL, sR, sC, sums, 1, eps, xh, rows_p, cols_p,
+                                       st->sms, s);
+    case PS_BF16:
+      return launch_norm_pass2<__nv_bfloat16>(x, L, rows, cols, sL, sR, sC, sums, 1, eps, xh, rows_p,
+                                              cols_p, st->sms, s);
+    case PS_F32:
+      return launch_norm_pass2<float>(x, L, rows, cols, sL, sR, sC, sums, 1, eps, xh, rows_p, cols_p,
+                                      st->sms, s);
+    default:
+      return launch_norm_pass2<double>(x, L, rows, cols, sL, sR, sC, sums, 1, eps, xh, rows_p, cols_p,
+                                       st->sms, s);
+  }
+}
+
+int ps_gram_f32(const void* x, float* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,
+                void* stream) {
+  if (!x || !out) return fail(PS_ERR_INVALID, "ps_gram_f32: null pointer");
+  if (!dims_ok(L, rows, cols) || x_ld < cols) return fail(PS_ERR_INVALID, "ps_gram_f32: bad sizes");
+  if (x_ld % 8) return fail(PS_ERR_INVALID, "ps_gram_f32: x_ld must be a multiple of 8");
+  if (!aligned16(x) || !aligned16(out))
+    return fail(PS_ERR_INVALID, "ps_gram_f32: pointers must be 16-byte aligned");
+  const bool tall = rows > cols;
+  const int64_t n = tall ? cols : rows, K = tall ? rows : cols;
+  if (n % 8) return fail(PS_ERR_INVALID, "ps_gram_f32: min(rows, cols) must be a multiple of 8");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb, td;
+  int rc;
+  if ((rc = map_out(&td, out, PS_F32, n, n, L, n, n * n))) return rc;
+  // The full n x n product on general tiles, FP32 out: no rounding, so the
+  // sum of such partial Grams can be rounded once.
+  ps::GemmArgs a = base_args(n, n, K, L);
+  fill_gen_tiles(a, n, n, L);
+  const double flops = 2.0 * L * n * n * K;
+  const double bytes = static_cast<double>(L) * (2.0 * n * K + 4.0 * n * n);
+  if (!tall) {
+    if ((rc = map_kmajor(&ta, x, K, n, L, x_ld, rows * x_ld, ps::BM))) return rc;
+    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, b_box_rows(false)))) return rc;
+    return launch_gemm<false, false, false, ps::kOutF32>(9, ta, tb, td, a, s, kProfGram, flops, bytes,
+                                                         false);
+  }
+  if ((rc = map_mnmajor(&ta, x, n, K, L, x_ld, rows * x_ld))) return rc;
+  return launch_gemm<true, true, false, ps::kOutF32>(10, ta, ta, td, a, s, kProfGram, flops, bytes,
+                                                     false);
 }
 
 int ps_gram(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,

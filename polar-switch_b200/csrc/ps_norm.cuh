@@ -144,9 +144,10 @@ __device__ __forceinline__ double chunk_sumsq(const T* p, long long n, double* s
   return block_sum(static_cast<double>(a), s_warp);
 }
 
-// Denominator of one matrix from its `nch` chunk sums; called by one full
-// warp, valid in every lane. Loads run ahead of the (ordered) additions.
-__device__ __forceinline__ float norm_den(const double* partial_m, int nch, float eps) {
+// Sum of one matrix's `nch` chunk sums in a fixed order (lane i adds chunks
+// i, i + 32, ..., then a fixed shuffle tree); called by one full warp, valid in
+// every lane. Loads run ahead of the (ordered) additions.
+__device__ __forceinline__ double ordered_sum(const double* partial_m, int nch) {
   const int lane = threadIdx.x & 31;
   double s = 0.0;
   int i = lane;
@@ -160,8 +161,22 @@ __device__ __forceinline__ float norm_den(const double* partial_m, int nch, floa
   for (; i < nch; i += 32) s += partial_m[i];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float nrm = static_cast<float>(sqrt(s));
+  return s;
+}
+
+// Denominator ||X||_F + eps of one matrix from its chunk sums (one full warp).
+__device__ __forceinline__ float norm_den(const double* partial_m, int nch, float eps) {
+  const float nrm = static_cast<float>(sqrt(ordered_sum(partial_m, nch)));
   return nrm + eps;  // FP32 add, as X.norm(...) + epsilon
+}
+
+// sums[l] = ordered_sum of matrix l's chunk sums (one warp per matrix).
+__global__ void ps_sum_partials_kernel(const double* __restrict__ partial, int chunks, long long L,
+                                       double* __restrict__ sums) {
+  const long long l = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (l >= L) return;
+  const double s = ordered_sum(partial + l * chunks, chunks);
+  if ((threadIdx.x & 31) == 0) sums[l] = s;
 }
 
 // Pass 1: partial[l * chunks + chunk] = sum of squares of one chunk of matrix l.
@@ -231,7 +246,9 @@ __global__ void __launch_bounds__(NORM_THREADS)
   __shared__ float s_den;
   const int l = blockIdx.y;
   if (threadIdx.x < 32) {
-    const float den = norm_den(partial + static_cast<long long>(l) * chunks, chunks, eps);
+    // No partial sums: a plain FP16 rounding (denominator 1).
+    const float den = partial ? norm_den(partial + static_cast<long long>(l) * chunks, chunks, eps)
+                              : 1.0f;
     if (threadIdx.x == 0) s_den = den;
   }
   __syncthreads();

@@ -155,3 +155,66 @@ def normalize(X, epsilon, out=None):
             nat.ptr(W), nat.DTYPE_CODES[X.dtype], L, rows, cols, sL, sR, sC, float(epsilon),
             nat.ptr(out), rows, cols, nat.ptr(ws), ws_bytes, nat.stream_ptr(X.device)))
     return out.reshape(X.shape)
+
+
+# ---------------------------------------------------------------- split matrices
+# The pieces of a circuit whose matrix is split by columns (rows when tall)
+# across ranks: the sums of squares and the Gram are partial on each rank and
+# are summed across the ranks between these calls.
+
+def sumsq(X):
+    """Per-matrix sum of squares of X (..., rows, cols), any strides, as FP64 (L,)."""
+    if not isinstance(X, torch.Tensor) or not X.is_cuda:
+        raise NotImplementedError("sumsq: polar_switch_b200 runs on CUDA tensors only")
+    if X.dtype not in nat.DTYPE_CODES:
+        raise TypeError(f"sumsq: unsupported dtype {X.dtype}")
+    W = _batched(X)
+    L, rows, cols = W.shape
+    sums = torch.empty(L, device=X.device, dtype=torch.float64)
+    lib = nat.load()
+    with torch.cuda.device(X.device):
+        ws_bytes = lib.ps_normalize_workspace_bytes(L, rows, cols)
+        ws = torch.empty(max(ws_bytes, 16), device=X.device, dtype=torch.uint8)
+        sL, sR, sC = W.stride()
+        nat.check("ps_sumsq", lib.ps_sumsq(nat.ptr(W), nat.DTYPE_CODES[X.dtype], L, rows, cols, sL, sR, sC,
+                                            nat.ptr(sums), nat.ptr(ws), ws_bytes, nat.stream_ptr(X.device)))
+    return sums
+
+
+def scale_cast(X, sums, epsilon, out=None):
+    """fp16(X / (sqrt(sums) + epsilon)) per matrix; ``sums`` None: plain FP16 rounding."""
+    if not isinstance(X, torch.Tensor) or not X.is_cuda:
+        raise NotImplementedError("scale_cast: polar_switch_b200 runs on CUDA tensors only")
+    if X.dtype not in nat.DTYPE_CODES:
+        raise TypeError(f"scale_cast: unsupported dtype {X.dtype}")
+    W = _batched(X)
+    L, rows, cols = W.shape
+    if sums is not None:
+        _require(sums, "scale_cast sums", torch.float64)
+        if sums.numel() != L:
+            raise ValueError("scale_cast: one sum per matrix")
+    if out is None:
+        out = torch.empty(W.shape, device=X.device, dtype=torch.float16)
+    _require(out, "scale_cast out")
+    with torch.cuda.device(X.device):
+        sL, sR, sC = W.stride()
+        nat.check("ps_scale_cast", nat.load().ps_scale_cast(
+            nat.ptr(W), nat.DTYPE_CODES[X.dtype], L, rows, cols, sL, sR, sC,
+            nat.ptr(sums) if sums is not None else None, float(epsilon), nat.ptr(out), rows, cols,
+            nat.stream_ptr(X.device)))
+    return out.reshape(X.shape)
+
+
+def gram_f32(X, out=None):
+    """X @ X.T (X.T @ X when tall) of FP16 X in FP32, not rounded, all n x n elements."""
+    _require(X, "gram_f32 X")
+    rows, cols = X.shape[-2:]
+    n = min(rows, cols)
+    L = X.numel() // (rows * cols)
+    if out is None:
+        out = torch.empty((*X.shape[:-2], n, n), device=X.device, dtype=torch.float32)
+    _require(out, "gram_f32 out", torch.float32)
+    with torch.cuda.device(X.device):
+        nat.check("ps_gram_f32", nat.load().ps_gram_f32(nat.ptr(X), nat.ptr(out), L, rows, cols, cols,
+                                                        nat.stream_ptr(X.device)))
+    return out

@@ -452,6 +452,213 @@ class ShardedOrthogonalizer:
         return res
 
 
+def split_plan(bank_shapes, world_size):
+    """Whether and how to split matrices across ranks: with fewer matrices than
+    ranks (the 4 x 8192 x 28672 stress batch on 8 GPUs), whole-matrix shards
+    would leave ranks idle, so each matrix is cut along its long dimension into
+    world_size / M parts, one per rank. Returns None (shard whole matrices) or
+    (parts per matrix, part length), the length a multiple of 8."""
+    M = sum(L for L, _, _ in bank_shapes)
+    if world_size < 2 or M >= world_size or world_size % M:
+        return None
+    parts = world_size // M
+    longest = max(max(r, c) for _, r, c in bank_shapes)
+    if any(max(r, c) != longest for _, r, c in bank_shapes):
+        return None  # one part length for every matrix keeps the plan simple
+    if any(r % 8 or c % 8 for _, r, c in bank_shapes):
+        return None  # parts of whole 16-byte rows, no padding
+    length = -(-(-(-longest // parts)) // 8) * 8
+    last = longest - (parts - 1) * length
+    for _, r, c in bank_shapes:
+        n = min(r, c)
+        # every part keeps the matrix's orientation (tall parts stay taller
+        # than wide, wide parts at least square), so the kernels treat a part
+        # exactly like the whole matrix
+        if last <= 0 or (r > c and last <= n) or (r <= c and last < n):
+            return None
+    return parts, length
+
+
+class SplitOrthogonalizer:
+    """Orthogonalize fewer matrices than ranks: each matrix is cut along its
+    long dimension (columns of a wide matrix, rows of a tall one) into one part
+    per rank of its group. Per outer iteration the ranks of a group sum their
+    partial FP32 Grams (an all-reduce of n x n, the one exchange step), round
+    once to FP16, run the inner iterations on the replicated n x n buffers and
+    apply them to their own part; the normalisation sums the parts' sums of
+    squares the same way. The result parts are then gathered like whole
+    matrices. Same interface as ShardedOrthogonalizer.
+
+    ``ops`` supplies sumsq / scale_cast / gram_f32 / square / apply (default:
+    the B200 kernels of polar_switch.cuda_ops; the CPU tests pass an oracle).
+    """
+
+    def __init__(self, bank_shapes, method="PS2_55", epsilon=1e-7, group=None, device=None,
+                 world_size=None, rank=None, ops=None, transport="auto"):
+        if world_size is None:
+            world_size = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        if rank is None:
+            rank = dist.get_rank(group) if world_size > 1 else 0
+        self.world_size, self.rank, self.group = world_size, rank, group
+        self.bank_shapes = [tuple(int(v) for v in s) for s in bank_shapes]
+        plan = split_plan(self.bank_shapes, world_size)
+        if plan is None:
+            raise ValueError("these banks do not split evenly across the ranks")
+        self.parts, self.length = plan
+        self.polar = make_polynomial_orthogonalizer(method, epsilon=epsilon)
+        self.table, self.epsilon = self.polar.table, epsilon
+        if ops is None:
+            from . import cuda_ops as ops
+        self.ops = ops
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.matrices = [(g, i) for g, (L, _, _) in enumerate(self.bank_shapes) for i in range(L)]
+        self.matrix = rank // self.parts
+        self.part = rank % self.parts
+        # One process group per matrix; every rank creates all of them, in order.
+        self.groups = []
+        for m in range(len(self.matrices)):
+            ranks = list(range(m * self.parts, (m + 1) * self.parts))
+            self.groups.append(dist.new_group(ranks) if world_size > 1 else None)
+        g, _ = self.matrices[self.matrix]
+        _, rows, cols = self.bank_shapes[g]
+        self.tall = rows > cols
+        self.n = min(rows, cols)
+        lo = self.part * self.length
+        hi = min(max(rows, cols), lo + self.length)
+        self.span = (lo, hi)
+        seg = self.n * self.length
+        self.seg = -(-seg // 128) * 128
+        if transport == "auto":
+            transport = "collective"
+        if transport != "collective":
+            raise ValueError("split matrices are gathered with the collective transport")
+        self.transport = transport
+        self.recv = torch.empty(world_size * self.seg, device=self.device, dtype=torch.float16)
+        table = self.table
+        self.flops_total = sum(L * circuit_flops(table, r, c) for L, r, c in self.bank_shapes)
+        self.plans = [{"pieces": [], "seg": self.seg, "offset": 0}]
+
+    def _part_view(self, X, part, tall):
+        lo = part * self.length
+        hi = min(X.shape[-2] if tall else X.shape[-1], lo + self.length)
+        return X[lo:hi, :] if tall else X[:, lo:hi]
+
+    def _check(self, banks):
+        if len(banks) != len(self.bank_shapes):
+            raise ValueError("expected one tensor per bank")
+        for X, shape in zip(banks, self.bank_shapes):
+            if tuple(X.shape) != shape:
+                raise ValueError(f"bank shape {tuple(X.shape)} does not match the plan {shape}")
+
+    def compute_local(self, banks):
+        """Orthogonalize this rank's part of its matrix into its segment of recv."""
+        ops, grp = self.ops, self.groups[self.matrix]
+        g, i = self.matrices[self.matrix]
+        Xj = self._part_view(banks[g][i], self.part, self.tall)
+        sums = ops.sumsq(Xj[None])
+        if self.world_size > 1:
+            dist.all_reduce(sums, group=grp)
+        Xh = ops.scale_cast(Xj[None], sums, self.epsilon)
+        n = self.n
+        buffers = 1 + max(max(w, s, a) for _, steps in self.table for w, s, a, *_ in steps)
+        work = [torch.empty((1, n, n), device=Xh.device, dtype=torch.float16) for _ in range(buffers)]
+        for residual, steps in self.table:
+            G = ops.gram_f32(Xh)
+            if self.world_size > 1:
+                dist.all_reduce(G, group=grp)
+            work[0] = ops.scale_cast(G, None, 0.0)
+            for dst, src, add, alpha, beta, diag in steps:
+                ops.square(work[src], work[add], work[dst], alpha, beta, diag)
+            Xh = ops.apply(Xh, work[steps[-1][0]], self.tall, residual)
+        flat = Xh.reshape(-1)
+        self.recv[self.rank * self.seg:self.rank * self.seg + flat.numel()].copy_(flat)
+        return self.recv
+
+    def __call__(self, banks):
+        """Orthogonalize all banks across the group; returns the gathered FP16 buffer."""
+        self._check(banks)
+        self.compute_local(banks)
+        if self.world_size > 1:
+            dist.all_gather_into_tensor(self.recv, self.recv[self.rank * self.seg:(self.rank + 1) * self.seg],
+                                        group=self.group)
+        return self.recv
+
+    def local_ranges(self, rank=None):
+        """(bank, start, count) of the matrix whose part the rank orthogonalizes."""
+        rank = self.rank if rank is None else rank
+        g, i = self.matrices[rank // self.parts]
+        return [(g, i, 1)]
+
+    def gathered_banks(self):
+        """The full update of every bank as one FP16 tensor each (copies)."""
+        out = []
+        for g, (L, rows, cols) in enumerate(self.bank_shapes):
+            mats = []
+            for i in range(L):
+                m = self.matrices.index((g, i))
+                pieces = []
+                for part in range(self.parts):
+                    r = m * self.parts + part
+                    lo = part * self.length
+                    hi = min(max(rows, cols), lo + self.length)
+                    shape = (hi - lo, cols) if rows > cols else (rows, hi - lo)
+                    n_el = shape[0] * shape[1]
+                    pieces.append(self.recv[r * self.seg:r * self.seg + n_el].view(shape))
+                mats.append(torch.cat(pieces, dim=0 if rows > cols else 1))
+            out.append(torch.stack(mats))
+        return out
+
+    def step_host(self, host_banks, host_out=None):
+        """One step from pinned host banks: uploads this rank's matrix, computes
+        its part and downloads the gathered FP16 buffer into `host_out`."""
+        self._check(host_banks)
+        if getattr(self, "_dev_in", None) is None:
+            self._dev_in = [torch.empty(b.shape, dtype=b.dtype, device=self.device) for b in host_banks]
+        if host_out is None:
+            host_out = torch.empty(self.recv.numel(), dtype=torch.float16, pin_memory=True)
+        g, i = self.matrices[self.matrix]
+        self._dev_in[g][i].copy_(host_banks[g][i], non_blocking=True)
+        self(self._dev_in)
+        host_out.copy_(self.recv, non_blocking=True)
+        return host_out
+
+    def capture(self, banks, warmup=2):
+        """Record one step as a CUDA graph (see ShardedOrthogonalizer.capture)."""
+        for _ in range(warmup):
+            self(banks)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self(banks)
+        torch.cuda.synchronize(self.device)
+        self._graph = graph
+        return graph
+
+    def replay(self):
+        self._graph.replay()
+        return self.recv
+
+    def close(self):
+        for name in ("_graph", "_dev_in"):
+            if hasattr(self, name):
+                delattr(self, name)
+
+
+def make_sharded_orthogonalizer(bank_shapes, **kwargs):
+    """ShardedOrthogonalizer, or SplitOrthogonalizer when there are fewer
+    matrices than ranks and they split evenly (`split_plan`)."""
+    world = kwargs.get("world_size")
+    if world is None:
+        world = dist.get_world_size(kwargs.get("group")) if dist.is_available() and dist.is_initialized() else 1
+    if split_plan([tuple(int(v) for v in s) for s in bank_shapes], world) is not None:
+        keep = {k: v for k, v in kwargs.items()
+                if k in ("method", "epsilon", "group", "device", "world_size", "rank", "transport")}
+        if keep.get("transport") == "copy_engine":
+            keep["transport"] = "collective"
+        return SplitOrthogonalizer(bank_shapes, **keep)
+    return ShardedOrthogonalizer(bank_shapes, **kwargs)
+
+
 def qwen3_0_6b_banks(layers=28, hidden=1024):
     """Bank shapes of a Qwen3-0.6B Muon step (training/configs/qwen600m.json:26-34)."""
     inter = 3 * hidden

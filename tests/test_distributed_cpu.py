@@ -195,3 +195,93 @@ def test_auto_buckets_follow_the_model():
         # a schedule never ends before its transfer, nor before its compute
         t = simulate_buckets(fr, compute, gather)
         assert t >= gather and t >= compute + BUCKET_OVERHEAD_S
+
+
+class _OracleSplitOps:
+    """CPU stand-ins for the split-matrix kernels (test infrastructure)."""
+
+    @staticmethod
+    def sumsq(X):
+        return X.double().pow(2).sum(dim=(-2, -1))
+
+    @staticmethod
+    def scale_cast(X, sums, epsilon):
+        if sums is None:
+            return X.half()
+        den = sums.sqrt().float().reshape(-1, 1, 1) + epsilon
+        return (X.float() / den).half()
+
+    @staticmethod
+    def gram_f32(Xh):
+        Xa = Xh.float()
+        return Xa.mT @ Xa if Xh.shape[-2] > Xh.shape[-1] else Xa @ Xa.mT
+
+    @staticmethod
+    def square(A, C, out, alpha, beta, diag):
+        from oracle import circuit as oc
+        out.copy_(oc.square(A, C, alpha, beta, diag))
+        return out
+
+    @staticmethod
+    def apply(X, B, tall, residual):
+        from oracle import circuit as oc
+        return oc.apply(X, B, tall, residual)
+
+
+def _split_worker(rank, world, port, shapes, result_queue):
+    try:
+        import datetime
+        import torch.distributed as dist
+        from polar_switch.distributed import make_sharded_orthogonalizer
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+        g = torch.Generator().manual_seed(9)
+        banks = [torch.randn(*s, generator=g) for s in shapes]
+        step = make_sharded_orthogonalizer(shapes, method="PS2_55", device="cpu", world_size=world,
+                                           rank=rank, transport="collective")
+        step.ops = _OracleSplitOps
+        step(banks)
+        result_queue.put((rank, type(step).__name__, [f.clone() for f in step.gathered_banks()]))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        result_queue.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+@pytest.mark.parametrize("world,shapes", [(2, [(1, 64, 256)]), (4, [(2, 384, 96)])])
+def test_split_matrices_gloo_match_the_whole_circuit(world, shapes):
+    """Fewer matrices than ranks: each matrix is cut along its long side, the
+    partial sums of squares and partial Grams are all-reduced, and the gathered
+    result matches the FP64 circuit on the whole matrix within the tolerance
+    of the whole-matrix path (the partial FP32 Grams are summed in another
+    order, so the bits differ from an unsplit evaluation)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_worker, args=(r, world, port, shapes, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            rank, kind, res = q.get(timeout=180)
+            results[rank] = (kind, res)
+    finally:
+        for p in procs:
+            p.join(timeout=10)
+            if p.is_alive():
+                p.kill()
+    from oracle import circuit as oc
+    g = torch.Generator().manual_seed(9)
+    banks = [torch.randn(*s, generator=g) for s in shapes]
+    ref64 = [oc.run_circuit(b, coefficients.PS2_55, acc=torch.float64) for b in banks]
+    ref32 = [oc.run_circuit(b, coefficients.PS2_55) for b in banks]
+    for r in range(world):
+        kind, res = results[r]
+        assert not isinstance(res, str), res
+        assert kind == "SplitOrthogonalizer"
+        for got, e64, e32 in zip(res, ref64, ref32):
+            assert got.shape == e64.shape
+            floor = oc.relative_frobenius(e32, e64)
+            assert oc.relative_frobenius(got, e64) <= max(5e-3, 1.5 * floor)

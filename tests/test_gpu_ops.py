@@ -179,3 +179,38 @@ def test_sym_product_is_p_at_q(cuda_device):
     out = cuda_ops.sym_product(P.to(cuda_device), Q.to(cuda_device), None, alpha=1.0, beta=0.0)
     ref = oc.sym_product(P, Q, None, 1.0, 0.0)
     assert_fp16_close(out, ref, what="sym_product P@Q")
+
+
+@pytest.mark.parametrize("shape,dtype", [((3, 1024, 3072), torch.float32), ((2, 384, 128), torch.bfloat16),
+                                         ((4, 200, 72), torch.float16)])
+def test_sumsq_and_scale_cast_compose_to_normalize(cuda_device, shape, dtype):
+    """The two pieces of the split-matrix normalisation give ps_normalize's
+    bits when the sums are not split; without sums scale_cast is .half()."""
+    from polar_switch import cuda_ops
+    X = seeded(shape, 97, dtype=dtype, scale=2.0).to(cuda_device)
+    sums = cuda_ops.sumsq(X)
+    assert sums.dtype == torch.float64 and sums.shape == (shape[0],)
+    ref = X.double().pow(2).sum(dim=(-2, -1))
+    assert torch.allclose(sums, ref, rtol=1e-5)
+    assert torch.equal(cuda_ops.scale_cast(X, sums, 1e-7), cuda_ops.normalize(X, 1e-7))
+    G = torch.randn(2, 256, 256, device=cuda_device)
+    assert torch.equal(cuda_ops.scale_cast(G, None, 0.0), G.half())
+    part = X[..., : shape[-1] // 2]  # strided view, as a split matrix's part
+    assert torch.allclose(cuda_ops.sumsq(part), part.double().pow(2).sum(dim=(-2, -1)), rtol=1e-5)
+
+
+@pytest.mark.parametrize("shape", [(2, 256, 768), (1, 640, 128), (3, 136, 136)])
+def test_gram_f32_is_the_unrounded_gram(cuda_device, shape):
+    from polar_switch import cuda_ops
+    X = oc.normalize(seeded(shape, 98), 1e-7)
+    got = cuda_ops.gram_f32(X.to(cuda_device)).cpu()
+    Xa = X.double()
+    ref = Xa.mT @ Xa if shape[-2] > shape[-1] else Xa @ Xa.mT
+    assert got.dtype == torch.float32
+    # tensor-core FP32 accumulation: well inside one FP16 ulp (4.9e-4 relative)
+    assert float((got.double() - ref).norm() / ref.norm()) < 5e-4
+    assert torch.equal(got, got.mT)  # both triangles from the same products
+    # rounded once, it is the FP16 Gram of the symmetric kernel to within one ulp
+    fp16 = torch.empty(shape[0], min(shape[1:]), min(shape[1:]), device=cuda_device, dtype=torch.float16)
+    cuda_ops.gram(X.to(cuda_device), shape[-2] > shape[-1], fp16)
+    assert_fp16_close(got.half(), fp16.cpu(), max_ulps=1, max_mismatch=0.02, what=f"gram_f32 {shape}")
