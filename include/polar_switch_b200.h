@@ -116,7 +116,19 @@ PS_API int ps_scale_cast(const void* x, int x_dtype, int64_t L, int64_t rows, in
 PS_API int ps_gram_f32(const void* x, float* out, int64_t L, int64_t rows, int64_t cols,
                        int64_t x_ld, void* stream);
 
-/* Scratch bytes ps_gns needs/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
+/* Muon's step before the circuit for one bucket of `count` same-shape matrices
+ * of `elems` elements (replaces the momentum / Nesterov / stack / cast loop
+ * of training/muon.py:63-74): for every matrix i, with grads[i] and moms[i]
+ * device pointers of `dtype` (FP32, BF16 or FP16):
+ *   m <- fl(fl(m * mu) + g);  d = fl(g + mu * m) (nesterov) or m;
+ *   out[i] = d cast to out_dtype, out being (count, elems) contiguous.
+ * The momentum buffers are updated in place; m and d are rounded to `dtype`
+ * where torch rounds them. `grads` and `moms` are host arrays of pointers. */
+PS_API int ps_muon_direction(const void* const* grads, void* const* moms, int count, int64_t elems,
+                             int dtype, float mu, int nesterov, void* out, int out_dtype,
+                             void* stream);
+
+/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 
 /* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch

@@ -19,6 +19,7 @@
 #include "ps_gemm.cuh"
 #include "ps_gemm2.cuh"
 #include "ps_norm.cuh"
+#include "ps_muon.cuh"
 
 namespace ps {
 // First error code recorded by a bounded wait in any kernel on this device.
@@ -920,6 +921,45 @@ int make_grouped_plan(const ps_problem* probs, int n_probs, int buffers, int sms
   return PS_OK;
 }
 
+template <typename T, typename TO>
+int launch_muon_direction(const void* const* grads, void* const* moms, int count, int64_t E,
+                          float mu, int nesterov, void* out, int sms, cudaStream_t s) {
+  for (int i0 = 0; i0 < count; i0 += ps::MUON_MAX_PARAMS) {
+    const int n = count - i0 < ps::MUON_MAX_PARAMS ? count - i0 : ps::MUON_MAX_PARAMS;
+    ps::MuonDirectionArgs a;
+    std::memset(&a, 0, sizeof(a));
+    for (int i = 0; i < n; ++i) {
+      a.grad[i] = grads[i0 + i];
+      a.mom[i] = moms[i0 + i];
+    }
+    a.E = E;
+    a.mu = mu;
+    a.nesterov = nesterov;
+    int64_t gx = (E + ps::NORM_THREADS * 4 - 1) / (ps::NORM_THREADS * 4);
+    const int64_t cap = (8LL * sms + n - 1) / n;
+    if (gx > cap) gx = cap;
+    if (gx < 1) gx = 1;
+    LaunchScope scope(kProfOther, s, 3.0 * n * E, static_cast<double>(n) * E * (3.0 * sizeof(T) + sizeof(TO)));
+    ps::ps_muon_direction_kernel<T, TO><<<dim3(static_cast<unsigned>(gx), n), ps::NORM_THREADS, 0, s>>>(
+        a, static_cast<TO*>(out) + static_cast<int64_t>(i0) * E);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "muon direction launch");
+  }
+  return PS_OK;
+}
+
+template <typename T>
+int muon_direction_out(int out_dtype, const void* const* grads, void* const* moms, int count, int64_t E,
+                       float mu, int nesterov, void* out, int sms, cudaStream_t s) {
+  switch (out_dtype) {
+    case PS_F16:
+      return launch_muon_direction<T, __half>(grads, moms, count, E, mu, nesterov, out, sms, s);
+    case PS_BF16:
+      return launch_muon_direction<T, __nv_bfloat16>(grads, moms, count, E, mu, nesterov, out, sms, s);
+    default:
+      return launch_muon_direction<T, float>(grads, moms, count, E, mu, nesterov, out, sms, s);
+  }
+}
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1125,6 +1165,32 @@ int ps_gram_f32(const void* x, float* out, int64_t L, int64_t rows, int64_t cols
   if ((rc = map_mnmajor(&ta, x, n, K, L, x_ld, rows * x_ld))) return rc;
   return launch_gemm<true, true, false, ps::kOutF32>(10, ta, ta, td, a, s, kProfGram, flops, bytes,
                                                      false);
+}
+
+int ps_muon_direction(const void* const* grads, void* const* moms, int count, int64_t elems,
+                      int dtype, float mu, int nesterov, void* out, int out_dtype, void* stream) {
+  if (!grads || !moms || !out) return fail(PS_ERR_INVALID, "ps_muon_direction: null pointer");
+  if (count < 1 || elems < 1) return fail(PS_ERR_INVALID, "ps_muon_direction: empty bucket");
+  for (int i = 0; i < count; ++i)
+    if (!grads[i] || !moms[i]) return fail(PS_ERR_INVALID, "ps_muon_direction: null matrix %d", i);
+  if (dtype != PS_F32 && dtype != PS_BF16 && dtype != PS_F16)
+    return fail(PS_ERR_INVALID, "ps_muon_direction: parameters must be FP32, BF16 or FP16");
+  if (out_dtype != PS_F32 && out_dtype != PS_BF16 && out_dtype != PS_F16)
+    return fail(PS_ERR_INVALID, "ps_muon_direction: the output must be FP32, BF16 or FP16");
+  if (!std::isfinite(mu)) return fail(PS_ERR_INVALID, "ps_muon_direction: momentum must be finite");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PS_F32:
+      return muon_direction_out<float>(out_dtype, grads, moms, count, elems, mu, nesterov, out, st->sms, s);
+    case PS_BF16:
+      return muon_direction_out<__nv_bfloat16>(out_dtype, grads, moms, count, elems, mu, nesterov, out,
+                                               st->sms, s);
+    default:
+      return muon_direction_out<__half>(out_dtype, grads, moms, count, elems, mu, nesterov, out, st->sms, s);
+  }
 }
 
 int ps_gram(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, int64_t x_ld,

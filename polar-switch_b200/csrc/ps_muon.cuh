@@ -1,0 +1,80 @@
+// Muon's step before the circuit (training/muon.py:63-74) for a bucket of
+// same-shape matrices, in one pass over their gradients and momentum buffers:
+//
+//   m <- fl(fl(m * mu) + g)            buf.mul_(momentum).add_(grad)
+//   d  = fl(g + mu * m)   (Nesterov)   grad.add(buf, alpha=momentum)
+//      = m                (plain)
+//   out[p] = cast(d)                   torch.stack(directions) [.bfloat16()]
+//
+// m and d are rounded to the parameters' dtype T exactly where torch rounds
+// them (after the multiply, after the add, after `g + mu * m`, evaluated in
+// FP32), then d is cast to the output dtype. The unfused sequence reads and
+// writes each element of the momentum, the gradient, the direction and the
+// stacked copy several times; here each is touched once.
+#pragma once
+
+#include "ps_norm.cuh"
+
+namespace ps {
+
+constexpr int MUON_MAX_PARAMS = 64;
+
+struct MuonDirectionArgs {
+  const void* grad[MUON_MAX_PARAMS];
+  void* mom[MUON_MAX_PARAMS];
+  long long E;       // elements per matrix
+  float mu;
+  int nesterov;
+};
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v);
+template <>
+__device__ __forceinline__ float round_to<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float round_to<__nv_bfloat16>(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+template <>
+__device__ __forceinline__ float round_to<__half>(float v) {
+  return __half2float(__float2half_rn(v));
+}
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) {
+  return __float2half_rn(v);
+}
+
+// grid (x: blocks over the elements, y: matrices of this launch)
+template <typename T, typename TO>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_muon_direction_kernel(const __grid_constant__ MuonDirectionArgs a, TO* __restrict__ out) {
+  const int p = blockIdx.y;
+  const T* g = static_cast<const T*>(a.grad[p]);
+  T* m = static_cast<T*>(a.mom[p]);
+  TO* o = out + static_cast<long long>(p) * a.E;
+  const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
+  for (long long e = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < a.E;
+       e += stride) {
+    const float gv = to_f32(g[e]);
+    const float m1 = round_to<T>(__fmul_rn(to_f32(m[e]), a.mu));
+    const float m2 = round_to<T>(__fadd_rn(m1, gv));
+    m[e] = from_f32<T>(m2);
+    const float d = a.nesterov ? round_to<T>(__fmaf_rn(a.mu, m2, gv)) : m2;
+    o[e] = from_f32<TO>(d);
+  }
+}
+
+}  // namespace ps

@@ -112,3 +112,23 @@ def test_qwen_step_flops():
     total = sum(L * circuit_flops(coefficients.PS2_55, r, c) for L, r, c in qwen3_0_6b_banks())
     assert total == pytest.approx(4.81e12, rel=2e-3)
     assert sum(L for L, _, _ in qwen3_0_6b_banks()) == 196
+
+
+def test_muon_module_groups_parameters_on_cpu():
+    """The Muon optimizer's parameter grouping follows the reference and its
+    kernel path refuses CPU tensors (there is no CPU fallback)."""
+    from polar_switch.muon import muon_directions, parameter_groups
+
+    class Block(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed_tokens = torch.nn.Embedding(10, 8)
+            self.q_proj = torch.nn.Linear(8, 16, bias=True)
+            self.o_proj = torch.nn.Linear(16, 8, bias=False)
+
+    groups, scalars = parameter_groups(Block())
+    assert [g["role"] for g in groups] == ["o_proj", "q_proj"]
+    n_matrix = sum(len(g["params"]) for g in groups)
+    assert n_matrix == 2 and len(scalars) == 2  # embedding + q_proj bias
+    with pytest.raises(NotImplementedError):
+        muon_directions([torch.zeros(4, 4)], [torch.zeros(4, 4)], 0.9, torch.bfloat16)

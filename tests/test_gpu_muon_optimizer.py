@@ -1,0 +1,70 @@
+"""The B200 Muon optimizer: the fused momentum / Nesterov / stack / cast
+kernel against torch's elementwise sequence, and whole optimizer steps against
+the reference's update rule (training/muon.py:58-86, restated here)."""
+
+import math
+
+import pytest
+import torch
+
+from polar_switch import make_polynomial_orthogonalizer
+from polar_switch.muon import Muon, muon_directions
+from tests._util import fp16_ulp, seeded
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype,out_dtype", [(torch.float32, torch.bfloat16), (torch.float32, torch.float32),
+                                             (torch.bfloat16, torch.bfloat16)])
+def test_fused_directions_match_torch(cuda_device, dtype, out_dtype):
+    mu = 0.95
+    grads = [seeded((192, 320), 400 + i, dtype=dtype).to(cuda_device) for i in range(5)]
+    moms = [seeded((192, 320), 410 + i, dtype=dtype).to(cuda_device) for i in range(5)]
+    ref_moms = [m.clone() for m in moms]
+    ref_dirs = []
+    for g, m in zip(grads, ref_moms):
+        m.mul_(mu).add_(g)
+        ref_dirs.append(g.add(m, alpha=mu))
+    ref = torch.stack(ref_dirs).to(out_dtype)
+    got = muon_directions(grads, moms, mu, out_dtype)
+    for m, r in zip(moms, ref_moms):
+        assert torch.equal(m, r)  # the momentum is rounded exactly where torch rounds it
+    assert got.shape == ref.shape and got.dtype == out_dtype
+    # g + mu * m may or may not be contracted into one FMA by torch: one rounding step apart at most
+    g32, r32 = got.float(), ref.float()
+    step = (fp16_ulp(r32) / 8) if out_dtype == torch.float32 else torch.pow(
+        2.0, torch.floor(torch.log2(r32.abs().clamp_min(2.0 ** -126))) - 7)
+    assert ((g32 - r32).abs() <= step + 1e-30).all()
+    assert float((g32 != r32).float().mean()) < 0.01
+
+
+def _reference_step(params, grads, moms, polar, lr, mu, wd):
+    """training/muon.py:63-86 for one bucket of the "rms" scale."""
+    directions = []
+    for g, m in zip(grads, moms):
+        m.mul_(mu).add_(g)
+        directions.append(g.add(m, alpha=mu))
+    update = polar(torch.stack(directions).bfloat16()).clone()
+    rows, cols = params[0].shape
+    factor = 0.2 * math.sqrt(max(rows, cols))
+    for p, u in zip(params, update.unbind()):
+        p.mul_(1 - lr * wd)
+        p.add_(u.to(p.dtype), alpha=-lr * factor)
+
+
+def test_optimizer_steps_follow_the_reference_rule(cuda_device):
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    shapes = [(256, 512)] * 3 + [(384, 128)] * 2
+    params = [torch.nn.Parameter(seeded(s, 420 + i).to(cuda_device) * 0.02) for i, s in enumerate(shapes)]
+    ref_params = [p.detach().clone() for p in params]
+    ref_moms = [torch.zeros_like(p) for p in ref_params]
+    opt = Muon([{"params": params, "role": "mlp"}], polar, lr=0.02, weight_decay=0.1)
+    for step in range(2):
+        grads = [seeded(s, 440 + 10 * step + i).to(cuda_device) for i, s in enumerate(shapes)]
+        for p, g in zip(params, grads):
+            p.grad = g.clone()
+        opt.step()
+        for lo, hi in ((0, 3), (3, 5)):
+            _reference_step(ref_params[lo:hi], grads[lo:hi], ref_moms[lo:hi], polar, 0.02, 0.95, 0.1)
+    for p, r in zip(params, ref_params):
+        assert float((p.detach() - r).norm() / r.norm()) < 1e-3
