@@ -128,7 +128,17 @@ PS_API int ps_muon_direction(const void* const* grads, void* const* moms, int co
                              int dtype, float mu, int nesterov, void* out, int out_dtype,
                              void* stream);
 
-/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
+/* Muon's step after the circuit for one bucket (replaces training/muon.py:84-86):
+ * for every matrix i (params[i] a device pointer of `dtype`, updates a
+ * (count, elems) contiguous array of `upd_dtype`):
+ *   p <- fl(fl(p * decay) + alpha * fl(u[i]))   decay = 1 - lr * wd,
+ *                                               alpha = -lr * scale factor,
+ * rounding to `dtype` where torch rounds. `params` is a host array. */
+PS_API int ps_muon_update(void* const* params, int count, int64_t elems, int dtype,
+                          const void* updates, int upd_dtype, float decay, float alpha,
+                          void* stream);
+
+/* Scratch bytes ps_gns needs/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 
 /* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch

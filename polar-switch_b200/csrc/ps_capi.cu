@@ -960,6 +960,43 @@ int muon_direction_out(int out_dtype, const void* const* grads, void* const* mom
       return launch_muon_direction<T, float>(grads, moms, count, E, mu, nesterov, out, sms, s);
   }
 }
+template <typename T, typename TU>
+int launch_muon_update(void* const* params, int count, int64_t E, float decay, float alpha,
+                       const void* upd, int sms, cudaStream_t s) {
+  for (int i0 = 0; i0 < count; i0 += ps::MUON_MAX_PARAMS) {
+    const int n = count - i0 < ps::MUON_MAX_PARAMS ? count - i0 : ps::MUON_MAX_PARAMS;
+    ps::MuonUpdateArgs a;
+    std::memset(&a, 0, sizeof(a));
+    for (int i = 0; i < n; ++i) a.param[i] = params[i0 + i];
+    a.E = E;
+    a.decay = decay;
+    a.alpha = alpha;
+    int64_t gx = (E + ps::NORM_THREADS * 4 - 1) / (ps::NORM_THREADS * 4);
+    const int64_t cap = (8LL * sms + n - 1) / n;
+    if (gx > cap) gx = cap;
+    if (gx < 1) gx = 1;
+    LaunchScope scope(kProfOther, s, 3.0 * n * E, static_cast<double>(n) * E * (2.0 * sizeof(T) + sizeof(TU)));
+    ps::ps_muon_update_kernel<T, TU><<<dim3(static_cast<unsigned>(gx), n), ps::NORM_THREADS, 0, s>>>(
+        a, static_cast<const TU*>(upd) + static_cast<int64_t>(i0) * E);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "muon update launch");
+  }
+  return PS_OK;
+}
+
+template <typename T>
+int muon_update_in(int upd_dtype, void* const* params, int count, int64_t E, float decay, float alpha,
+                   const void* upd, int sms, cudaStream_t s) {
+  switch (upd_dtype) {
+    case PS_F16:
+      return launch_muon_update<T, __half>(params, count, E, decay, alpha, upd, sms, s);
+    case PS_BF16:
+      return launch_muon_update<T, __nv_bfloat16>(params, count, E, decay, alpha, upd, sms, s);
+    default:
+      return launch_muon_update<T, float>(params, count, E, decay, alpha, upd, sms, s);
+  }
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1190,6 +1227,32 @@ int ps_muon_direction(const void* const* grads, void* const* moms, int count, in
                                                st->sms, s);
     default:
       return muon_direction_out<__half>(out_dtype, grads, moms, count, elems, mu, nesterov, out, st->sms, s);
+  }
+}
+
+int ps_muon_update(void* const* params, int count, int64_t elems, int dtype, const void* updates,
+                   int upd_dtype, float decay, float alpha, void* stream) {
+  if (!params || !updates) return fail(PS_ERR_INVALID, "ps_muon_update: null pointer");
+  if (count < 1 || elems < 1) return fail(PS_ERR_INVALID, "ps_muon_update: empty bucket");
+  for (int i = 0; i < count; ++i)
+    if (!params[i]) return fail(PS_ERR_INVALID, "ps_muon_update: null matrix %d", i);
+  if (dtype != PS_F32 && dtype != PS_BF16 && dtype != PS_F16)
+    return fail(PS_ERR_INVALID, "ps_muon_update: parameters must be FP32, BF16 or FP16");
+  if (upd_dtype != PS_F32 && upd_dtype != PS_BF16 && upd_dtype != PS_F16)
+    return fail(PS_ERR_INVALID, "ps_muon_update: updates must be FP32, BF16 or FP16");
+  if (!std::isfinite(decay) || !std::isfinite(alpha))
+    return fail(PS_ERR_INVALID, "ps_muon_update: factors must be finite");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PS_F32:
+      return muon_update_in<float>(upd_dtype, params, count, elems, decay, alpha, updates, st->sms, s);
+    case PS_BF16:
+      return muon_update_in<__nv_bfloat16>(upd_dtype, params, count, elems, decay, alpha, updates, st->sms, s);
+    default:
+      return muon_update_in<__half>(upd_dtype, params, count, elems, decay, alpha, updates, st->sms, s);
   }
 }
 

@@ -77,4 +77,29 @@ __global__ void __launch_bounds__(NORM_THREADS)
   }
 }
 
+// Muon's step after the circuit (training/muon.py:84-86) for a bucket:
+//   p <- fl(fl(p * decay) + alpha * fl_T(u[i]))
+// (p.mul_(1 - lr * wd); p.add_(u.to(p.dtype), alpha=-lr * factor)), with p of
+// dtype T rounded where torch rounds it and u the circuit's stacked output.
+struct MuonUpdateArgs {
+  void* param[MUON_MAX_PARAMS];
+  long long E;
+  float decay, alpha;
+};
+
+template <typename T, typename TU>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_muon_update_kernel(const __grid_constant__ MuonUpdateArgs a, const TU* __restrict__ upd) {
+  const int p = blockIdx.y;
+  T* w = static_cast<T*>(a.param[p]);
+  const TU* u = upd + static_cast<long long>(p) * a.E;
+  const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
+  for (long long e = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < a.E;
+       e += stride) {
+    const float w1 = round_to<T>(__fmul_rn(to_f32(w[e]), a.decay));
+    const float uv = round_to<T>(to_f32(u[e]));
+    w[e] = from_f32<T>(__fmaf_rn(a.alpha, uv, w1));
+  }
+}
+
 }  // namespace ps

@@ -11,7 +11,9 @@ weight decay and the scaled update. Two things differ in how it runs:
     elementwise passes per matrix;
   * when the orthogonalizer has ``grouped`` (every orthogonalizer of this
     package except GNS), all buckets of a parameter group are orthogonalized
-    in one grouped call.
+    in one grouped call;
+  * the decoupled weight decay and the scaled update are one kernel per
+    bucket (ps_muon_update) instead of three elementwise passes per matrix.
 
 `parameter_groups` is the reference's grouping (training/muon.py:14-28).
 """
@@ -53,6 +55,24 @@ def muon_directions(grads, moms, momentum, out_dtype, nesterov=True):
             gp, mp, len(grads), g0.numel(), nat.DTYPE_CODES[g0.dtype], float(momentum), 1 if nesterov else 0,
             nat.ptr(out), nat.DTYPE_CODES[out_dtype], nat.stream_ptr(g0.device)))
     return out
+
+
+def muon_update(params, update, decay, alpha):
+    """p <- p * decay + alpha * u for each matrix p and its row u of the stacked
+    `update`, rounded like torch's p.mul_(decay); p.add_(u.to(p.dtype), alpha)."""
+    p0 = params[0]
+    if not p0.is_cuda:
+        raise NotImplementedError("muon_update: polar_switch_b200 runs on CUDA tensors only")
+    for p in params:
+        if p.shape != p0.shape or p.dtype != p0.dtype or not p.is_contiguous() or p.device != p0.device:
+            raise ValueError("muon_update: a bucket needs contiguous tensors of one shape, dtype and device")
+    if update.shape != (len(params), *p0.shape) or not update.is_contiguous() or update.device != p0.device:
+        raise ValueError("muon_update: the update must be the stacked (count, *shape) result")
+    pp = (ctypes.c_void_p * len(params))(*[p.data_ptr() for p in params])
+    with torch.cuda.device(p0.device):
+        nat.check("ps_muon_update", nat.load().ps_muon_update(
+            pp, len(params), p0.numel(), nat.DTYPE_CODES[p0.dtype], nat.ptr(update),
+            nat.DTYPE_CODES[update.dtype], float(decay), float(alpha), nat.stream_ptr(p0.device)))
 
 
 class Muon(torch.optim.Optimizer):
@@ -99,6 +119,10 @@ class Muon(torch.optim.Optimizer):
                 rows, cols = params[0].shape
                 factor = (0.2 * math.sqrt(max(rows, cols)) if group["scale"] == "rms"
                           else math.sqrt(rows / cols))
-                for p, u in zip(params, update.unbind()):
-                    p.mul_(1 - group["lr"] * group["weight_decay"])
-                    p.add_(u.to(p.dtype), alpha=-group["lr"] * factor)
+                if all(p.is_contiguous() for p in params) and update.is_contiguous():
+                    muon_update(params, update, 1 - group["lr"] * group["weight_decay"],
+                                -group["lr"] * factor)
+                else:
+                    for p, u in zip(params, update.unbind()):
+                        p.mul_(1 - group["lr"] * group["weight_decay"])
+                        p.add_(u.to(p.dtype), alpha=-group["lr"] * factor)

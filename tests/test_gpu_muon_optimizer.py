@@ -38,6 +38,27 @@ def test_fused_directions_match_torch(cuda_device, dtype, out_dtype):
     assert float((g32 != r32).float().mean()) < 0.01
 
 
+@pytest.mark.parametrize("dtype,udtype", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                          (torch.float32, torch.float16)])
+def test_fused_update_matches_torch(cuda_device, dtype, udtype):
+    from polar_switch.muon import muon_update
+    params = [seeded((160, 264), 450 + i, dtype=dtype).to(cuda_device) for i in range(4)]
+    update = torch.stack([seeded((160, 264), 460 + i).to(cuda_device) for i in range(4)]).to(udtype)
+    ref = [p.clone() for p in params]
+    decay, alpha = 1 - 0.02 * 0.1, -0.02 * 3.7
+    for p, u in zip(ref, update.unbind()):
+        p.mul_(decay)
+        p.add_(u.to(p.dtype), alpha=alpha)
+    muon_update(params, update, decay, alpha)
+    for got, want in zip(params, ref):
+        g, w = got.float(), want.float()
+        # one rounding step of the parameter dtype at most (FMA or not in torch's add)
+        step = torch.pow(2.0, torch.floor(torch.log2(w.abs().clamp_min(2.0 ** -126)))
+                         - (23 if dtype == torch.float32 else 7))
+        assert ((g - w).abs() <= step).all()
+        assert float((g != w).float().mean()) < 0.01
+
+
 def _reference_step(params, grads, moms, polar, lr, mu, wd):
     """training/muon.py:63-86 for one bucket of the "rms" scale."""
     directions = []
