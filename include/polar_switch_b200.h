@@ -25,6 +25,11 @@
  *   polar_switch/gemm_symmetric_fused.py:304-309 / triton_kernels.py:82-87
  *                                           apply(X, B, tall, residual) -> ps_apply
  *   polar_switch/gram_newton_schulz.py:107  Q = Z + a*I          -> ps_add_diag
+ *   polar_switch/gram_newton_schulz.py:75-122 rectangular GNS     -> ps_gns
+ *   training/muon.py:59-86 (buckets of one step) -> ps_circuit_grouped
+ *   training/muon.py:63-74 momentum/Nesterov/stack/cast -> ps_muon_direction
+ *   training/muon.py:84-86 decay and scaled update     -> ps_muon_update
+ *   (no single counterpart) split-matrix pieces -> ps_sumsq, ps_scale_cast, ps_gram_f32
  */
 #ifndef POLAR_SWITCH_B200_H
 #define POLAR_SWITCH_B200_H
@@ -53,6 +58,7 @@ extern "C" {
 #define PS_BF16 2
 #define PS_F64 3
 
+
 /* One inner iteration (w, i, r, a, b, c) of a coefficient table:
  * B[dst] = alpha * B[src] @ B[src] + beta * B[add] + diag * I
  * (polar_switch/coefficients.py:1-8). */
@@ -76,6 +82,11 @@ PS_API int ps_get_status(int* status, int clear);
  * launched afterwards by this process (default 2^32, about two seconds). */
 PS_API int ps_set_wait_limit(long long cycles);
 
+/* Launches one kernel whose single wait can never be satisfied, so that it
+ * runs out after `limit_cycles` and records its status code (5). Used by the
+ * tests of the bounded-wait path. */
+PS_API int ps_selftest_wait(long long limit_cycles, void* stream);
+
 /* Number of kernels this library has launched in the process so far. */
 PS_API long long ps_launch_count(void);
 
@@ -96,74 +107,10 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
  * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);
 
-/* Pieces of the normalisation and of the Gram for a matrix split by columns
- * (or, tall, by rows) across ranks, the split Muon step for banks with fewer
- * matrices than ranks (no single counterpart in the reference; together they
- * replace polar_switch/__init__.py:34-35 and the Gram of :41 when the partial
- * results are summed across ranks between the calls):
- *   ps_sumsq: sums[l] = sum of squares of x[l] (FP64, the same chunks and
- *     order as ps_normalize); workspace of ps_normalize_workspace_bytes;
- *   ps_scale_cast: xh[l] = fp16(x[l] / (sqrt(sums[l]) + eps)), padding zeroed;
- *     sums == NULL gives a plain FP16 rounding (denominator 1);
- *   ps_gram_f32: out[l] = X X^T (X^T X when rows > cols) in FP32, not rounded,
- *     all n x n elements (general tiles). */
-PS_API int ps_sumsq(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
-                    int64_t sR, int64_t sC, double* sums, void* workspace, int64_t workspace_bytes,
-                    void* stream);
-PS_API int ps_scale_cast(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols,
-                         int64_t sL, int64_t sR, int64_t sC, const double* sums, float eps, void* xh,
-                         int64_t rows_p, int64_t cols_p, void* stream);
-PS_API int ps_gram_f32(const void* x, float* out, int64_t L, int64_t rows, int64_t cols,
-                       int64_t x_ld, void* stream);
-
-/* Muon's step before the circuit for one bucket of `count` same-shape matrices
- * of `elems` elements (replaces the momentum / Nesterov / stack / cast loop
- * of training/muon.py:63-74): for every matrix i, with grads[i] and moms[i]
- * device pointers of `dtype` (FP32, BF16 or FP16):
- *   m <- fl(fl(m * mu) + g);  d = fl(g + mu * m) (nesterov) or m;
- *   out[i] = d cast to out_dtype, out being (count, elems) contiguous.
- * The momentum buffers are updated in place; m and d are rounded to `dtype`
- * where torch rounds them. `grads` and `moms` are host arrays of pointers. */
-PS_API int ps_muon_direction(const void* const* grads, void* const* moms, int count, int64_t elems,
-                             int dtype, float mu, int nesterov, void* out, int out_dtype,
-                             void* stream);
-
-/* Muon's step after the circuit for one bucket (replaces training/muon.py:84-86):
- * for every matrix i (params[i] a device pointer of `dtype`, updates a
- * (count, elems) contiguous array of `upd_dtype`):
- *   p <- fl(fl(p * decay) + alpha * fl(u[i]))   decay = 1 - lr * wd,
- *                                               alpha = -lr * scale factor,
- * rounding to `dtype` where torch rounds. `params` is a host array. */
-PS_API int ps_muon_update(void* const* params, int count, int64_t elems, int dtype,
-                          const void* updates, int upd_dtype, float decay, float alpha,
-                          void* stream);
-
-/* Scratch bytes ps_gns needs/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
-PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
-
-/* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch
- * of polar_switch/gram_newton_schulz.py:75-122): normalise, R = X X^T (X^T X
- * when rows > cols), then for iteration i with coeffs[3i..3i+2] = (a, b, c):
- * Z = c R R + b R; Q = Z + a I at i = 0 and at restarts, else Q = Q Z + a Q;
- * before the next iteration (unless it restarts) R = Z (R Z + a R) + a (R Z
- * + a R); iteration i in `resets` (i > 0) first sets X <- Q X and R from it.
- * y = Q X (X Q when tall). Every product is one tcgen05 launch with FP32
- * accumulation and one FP16 rounding. Square matrices are rejected
- * (PS_ERR_INVALID): the reference sends them to Polar Express. */
-PS_API int ps_gns(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
-                  int64_t sR, int64_t sC, void* y, int y_dtype, int n_iter, const float* coeffs,
-                  int n_resets, const int32_t* resets, float eps, void* workspace,
-                  int64_t workspace_bytes, void* stream);
-
 /* Caps the number of CTAs/* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
  * afterwards; 0 (default) = every SM. Leaving SMs free lets a collective on
  * another stream run beside the GEMMs. Returns the previous cap. */
 PS_API int ps_set_max_ctas(int max_ctas);
-
-/* Launches one kernel whose single wait can never be satisfied, so that it
- * runs out after `limit_cycles` and records its status code (5). Used by the
- * tests of the bounded-wait path. */
-PS_API int ps_selftest_wait(long long limit_cycles, void* stream);
 
 /* Scratch bytes ps_normalize needs for L matrices of rows x cols. */
 PS_API int64_t ps_normalize_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
@@ -272,6 +219,65 @@ PS_API int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer,
                               const float* residuals, const int32_t* n_steps, const ps_step* steps,
                               int buffers, float eps, void* workspace, int64_t workspace_bytes,
                               void* stream);
+
+/* Scratch bytes ps_gns needs/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
+PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
+
+/* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch
+ * of polar_switch/gram_newton_schulz.py:75-122): normalise, R = X X^T (X^T X
+ * when rows > cols), then for iteration i with coeffs[3i..3i+2] = (a, b, c):
+ * Z = c R R + b R; Q = Z + a I at i = 0 and at restarts, else Q = Q Z + a Q;
+ * before the next iteration (unless it restarts) R = Z (R Z + a R) + a (R Z
+ * + a R); iteration i in `resets` (i > 0) first sets X <- Q X and R from it.
+ * y = Q X (X Q when tall). Every product is one tcgen05 launch with FP32
+ * accumulation and one FP16 rounding. Square matrices are rejected
+ * (PS_ERR_INVALID): the reference sends them to Polar Express. */
+PS_API int ps_gns(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                  int64_t sR, int64_t sC, void* y, int y_dtype, int n_iter, const float* coeffs,
+                  int n_resets, const int32_t* resets, float eps, void* workspace,
+                  int64_t workspace_bytes, void* stream);
+
+/* Pieces of the normalisation and of the Gram for a matrix split by columns
+ * (or, tall, by rows) across ranks, the split Muon step for banks with fewer
+ * matrices than ranks (no single counterpart in the reference; together they
+ * replace polar_switch/__init__.py:34-35 and the Gram of :41 when the partial
+ * results are summed across ranks between the calls):
+ *   ps_sumsq: sums[l] = sum of squares of x[l] (FP64, the same chunks and
+ *     order as ps_normalize); workspace of ps_normalize_workspace_bytes;
+ *   ps_scale_cast: xh[l] = fp16(x[l] / (sqrt(sums[l]) + eps)), padding zeroed;
+ *     sums == NULL gives a plain FP16 rounding (denominator 1);
+ *   ps_gram_f32: out[l] = X X^T (X^T X when rows > cols) in FP32, not rounded,
+ *     all n x n elements (general tiles). */
+PS_API int ps_sumsq(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols, int64_t sL,
+                    int64_t sR, int64_t sC, double* sums, void* workspace, int64_t workspace_bytes,
+                    void* stream);
+PS_API int ps_scale_cast(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t cols,
+                         int64_t sL, int64_t sR, int64_t sC, const double* sums, float eps, void* xh,
+                         int64_t rows_p, int64_t cols_p, void* stream);
+PS_API int ps_gram_f32(const void* x, float* out, int64_t L, int64_t rows, int64_t cols,
+                       int64_t x_ld, void* stream);
+
+/* Muon's step before the circuit for one bucket of `count` same-shape matrices
+ * of `elems` elements (replaces the momentum / Nesterov / stack / cast loop
+ * of training/muon.py:63-74): for every matrix i, with grads[i] and moms[i]
+ * device pointers of `dtype` (FP32, BF16 or FP16):
+ *   m <- fl(fl(m * mu) + g);  d = fl(g + mu * m) (nesterov) or m;
+ *   out[i] = d cast to out_dtype, out being (count, elems) contiguous.
+ * The momentum buffers are updated in place; m and d are rounded to `dtype`
+ * where torch rounds them. `grads` and `moms` are host arrays of pointers. */
+PS_API int ps_muon_direction(const void* const* grads, void* const* moms, int count, int64_t elems,
+                             int dtype, float mu, int nesterov, void* out, int out_dtype,
+                             void* stream);
+
+/* Muon's step after the circuit for one bucket (replaces training/muon.py:84-86):
+ * for every matrix i (params[i] a device pointer of `dtype`, updates a
+ * (count, elems) contiguous array of `upd_dtype`):
+ *   p <- fl(fl(p * decay) + alpha * fl(u[i]))   decay = 1 - lr * wd,
+ *                                               alpha = -lr * scale factor,
+ * rounding to `dtype` where torch rounds. `params` is a host array. */
+PS_API int ps_muon_update(void* const* params, int count, int64_t elems, int dtype,
+                          const void* updates, int upd_dtype, float decay, float alpha,
+                          void* stream);
 
 #ifdef __cplusplus
 }
