@@ -8,7 +8,9 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <atomic>
+#include <cstdint>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -789,6 +791,117 @@ int normalize_impl(const void* x, int x_dtype, int64_t L, int64_t rows, int64_t 
   }
 }
 
+// One normalisation of a grouped circuit: the arguments of normalize_impl.
+struct NormJob {
+  const void* x;
+  int x_dtype;
+  int64_t L, R, C, sL, sR, sC;
+  void* xh;
+  int64_t Rp, Cp;
+  double* partial;
+};
+
+// Both passes of up to NORM_BATCH_MAX normalisations with input type T, one
+// launch per pass. Each matrix keeps normalize_impl's chunk count and chunk
+// size, so its chunk sums, their ordered sum and every FP16 output are the
+// same bits as in a launch of its own; only the split of the scale-and-cast
+// pass into blocks differs (sized by each problem's share of the elements),
+// and no output depends on that split.
+template <typename T>
+int launch_normalize_batch(const NormJob* jobs, int n, float eps, int sms, cudaStream_t s) {
+  ps::NormBatch b1, b2;
+  std::memset(&b1, 0, sizeof(b1));
+  std::memset(&b2, 0, sizeof(b2));
+  b1.count = b2.count = n;
+  b1.eps = b2.eps = eps;
+  double elems = 0.0, in_bytes = 0.0, out_bytes = 0.0;
+  for (int i = 0; i < n; ++i) {
+    elems += static_cast<double>(jobs[i].L) * jobs[i].R * jobs[i].C;
+    out_bytes += 2.0 * jobs[i].L * jobs[i].Rp * jobs[i].Cp;
+  }
+  in_bytes = elems * sizeof(T);
+  int64_t blocks1 = 0, blocks2 = 0;
+  for (int i = 0; i < n; ++i) {
+    const NormJob& j = jobs[i];
+    const int flat = (j.sC == 1 && j.sR == j.C) ? 1 : 0;
+    const int64_t ce = ps::norm_chunk_elems(j.R * j.C);
+    int chunks = norm_chunks(j.L, j.R, j.C, sms);
+    if (flat) chunks = static_cast<int>((j.R * j.C + ce - 1) / ce);
+    for (ps::NormBatch* b : {&b1, &b2}) {
+      ps::NormBatchProblem& q = b->p[i];
+      q.x = j.x;
+      q.xh = static_cast<__half*>(j.xh);
+      q.partial = j.partial;
+      q.R = j.R;
+      q.C = j.C;
+      q.sL = j.sL;
+      q.sR = j.sR;
+      q.sC = j.sC;
+      q.Rp = j.Rp;
+      q.Cp = j.Cp;
+      q.chunk_elems = ce;
+      q.flat = flat;
+      q.chunks = chunks;
+    }
+    b1.p[i].b0 = blocks1;
+    b1.p[i].per = chunks;
+    blocks1 += j.L * chunks;
+    // About 4 blocks per SM over the whole launch, shared by element count.
+    const int64_t per_mat = (j.Rp * j.Cp + ps::NORM_THREADS * 8 - 1) / (ps::NORM_THREADS * 8);
+    const double share = static_cast<double>(j.L) * j.R * j.C / elems;
+    int64_t gx = static_cast<int64_t>(std::ceil(4.0 * sms * share / j.L));
+    if (gx > per_mat) gx = per_mat;
+    if (gx < 1) gx = 1;
+    b2.p[i].b0 = blocks2;
+    b2.p[i].per = gx;
+    blocks2 += j.L * gx;
+  }
+  if (blocks1 > INT32_MAX || blocks2 > INT32_MAX)
+    return fail(PS_ERR_INVALID, "ps_circuit: normalisation grid too large");
+  {
+    LaunchScope scope(kProfNormalize, s, 2.0 * elems, in_bytes);
+    ps::ps_norm_partial_batched_kernel<T>
+        <<<static_cast<unsigned>(blocks1), ps::NORM_THREADS, 0, s>>>(b1);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "normalize launch (batched pass 1)");
+  }
+  LaunchScope scope(kProfNormalize, s, elems, in_bytes + out_bytes);
+  ps::ps_scale_cast_batched_kernel<T><<<static_cast<unsigned>(blocks2), ps::NORM_THREADS, 0, s>>>(b2);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "normalize launch (batched pass 2)");
+}
+
+// The normalisations of a grouped circuit: jobs of one input type are batched
+// NORM_BATCH_MAX at a time; a type with a single job takes normalize_impl.
+int normalize_jobs(const std::vector<NormJob>& jobs, float eps, int sms, cudaStream_t s) {
+  if (!(eps > 0.f)) return fail(PS_ERR_INVALID, "ps_normalize: eps must be positive");
+  for (const NormJob& j : jobs)
+    if (elem_bytes(j.x_dtype) == 0) return fail(PS_ERR_INVALID, "ps_normalize: bad dtype");
+  for (int dt : {PS_F16, PS_BF16, PS_F32, PS_F64}) {
+    std::vector<NormJob> same;
+    for (const NormJob& j : jobs)
+      if (j.x_dtype == dt) same.push_back(j);
+    for (size_t i0 = 0; i0 < same.size(); i0 += ps::NORM_BATCH_MAX) {
+      const int n = static_cast<int>(std::min<size_t>(same.size() - i0, ps::NORM_BATCH_MAX));
+      const NormJob* b = same.data() + i0;
+      int rc;
+      if (n == 1) {
+        rc = normalize_impl(b->x, b->x_dtype, b->L, b->R, b->C, b->sL, b->sR, b->sC, eps, b->xh,
+                            b->Rp, b->Cp, b->partial, normalize_ws_bytes(b->L, b->R, b->C, sms), s);
+      } else {
+        switch (dt) {
+          case PS_F16: rc = launch_normalize_batch<__half>(b, n, eps, sms, s); break;
+          case PS_BF16: rc = launch_normalize_batch<__nv_bfloat16>(b, n, eps, sms, s); break;
+          case PS_F32: rc = launch_normalize_batch<float>(b, n, eps, sms, s); break;
+          default: rc = launch_normalize_batch<double>(b, n, eps, sms, s); break;
+        }
+      }
+      if (rc) return rc;
+    }
+  }
+  return PS_OK;
+}
+
 template <typename T>
 int launch_copy_out(const void* xh, int64_t Rp, int64_t Cp, int64_t R, int64_t C, int64_t L,
                     void* y, int sms, cudaStream_t s) {
@@ -1347,13 +1460,18 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
   // Square buffers live only inside this call, so they are kept as
   // upper-triangle blocks (no mirrored stores).
   const bool tri = true;
+  std::vector<NormJob> norm_jobs(np);
   for (int i = 0; i < np; ++i) {
     const ps_problem& q = probs[i];
     const GroupedPlan::Prob& p = plan.probs[i];
-    if ((rc = normalize_impl(q.x, q.x_dtype, q.L, q.rows, q.cols, q.sL, q.sR, q.sC, eps,
-                             ws + p.xh_off[0], p.lay.Rp, p.lay.Cp, ws + p.norm_off,
-                             p.lay.norm_bytes, s)))
-      return rc;
+    norm_jobs[i] = {q.x, q.x_dtype, q.L, q.rows, q.cols, q.sL, q.sR, q.sC, ws + p.xh_off[0],
+                    p.lay.Rp, p.lay.Cp, reinterpret_cast<double*>(ws + p.norm_off)};
+  }
+  // The normalisations of all problems, batched by input type.
+  if ((rc = normalize_jobs(norm_jobs, eps, st->sms, s))) return rc;
+  for (int i = 0; i < np; ++i) {
+    const ps_problem& q = probs[i];
+    const GroupedPlan::Prob& p = plan.probs[i];
     // The last apply writes straight into y when y's layout allows TMA stores.
     direct[i] = (q.y_dtype == PS_F16 || q.y_dtype == PS_F32 || q.y_dtype == PS_BF16) &&
                 p.lay.Rp == q.rows && p.lay.Cp == q.cols &&

@@ -183,13 +183,13 @@ __global__ void ps_sum_partials_kernel(const double* __restrict__ partial, int c
 // Contiguous matrices (`flat`) use the canonical chunks of `chunk_elems`
 // elements; strided ones are split into `chunks` row ranges.
 template <typename T>
-__global__ void __launch_bounds__(NORM_THREADS)
-    ps_norm_partial_kernel(const T* __restrict__ x, long long R, long long C, long long sL,
-                           long long sR, long long sC, int flat, int chunks, long long chunk_elems,
-                           double* __restrict__ partial) {
+__device__ __forceinline__ void norm_partial_body(const T* __restrict__ x, long long R, long long C,
+                                                  long long sL, long long sR, long long sC, int flat,
+                                                  int chunks, long long chunk_elems,
+                                                  double* __restrict__ partial, long long l,
+                                                  long long chunk) {
   __shared__ double s_warp[NORM_THREADS / 32];
-  const int l = blockIdx.y, chunk = blockIdx.x;
-  const T* xm = x + static_cast<long long>(l) * sL;
+  const T* xm = x + l * sL;
   double tot;
   if (flat) {
     const long long E = R * C;
@@ -209,7 +209,15 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
     tot = block_sum(acc, s_warp);
   }
-  if (threadIdx.x == 0) partial[static_cast<long long>(l) * chunks + chunk] = tot;
+  if (threadIdx.x == 0) partial[l * chunks + chunk] = tot;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_norm_partial_kernel(const T* __restrict__ x, long long R, long long C, long long sL,
+                           long long sR, long long sC, int flat, int chunks, long long chunk_elems,
+                           double* __restrict__ partial) {
+  norm_partial_body(x, R, C, sL, sR, sC, flat, chunks, chunk_elems, partial, blockIdx.y, blockIdx.x);
 }
 
 // 8 consecutive elements of T (16-byte aligned) as floats.
@@ -238,31 +246,31 @@ __device__ __forceinline__ uint4 scale8(const float (&f)[8], float den) {
 
 // Pass 2: Xh[l] (Rp x Cp, FP16, zero padding) = X[l] / (norm_l + eps).
 template <typename T>
-__global__ void __launch_bounds__(NORM_THREADS)
-    ps_scale_cast_kernel(const T* __restrict__ x, long long R, long long C, long long sL,
-                         long long sR, long long sC, int flat, const double* __restrict__ partial,
-                         int chunks, float eps, __half* __restrict__ xh, long long Rp,
-                         long long Cp) {
+__device__ __forceinline__ void scale_cast_body(const T* __restrict__ x, long long R, long long C,
+                                                long long sL, long long sR, long long sC, int flat,
+                                                const double* __restrict__ partial, int chunks,
+                                                float eps, __half* __restrict__ xh, long long Rp,
+                                                long long Cp, long long l, long long bx,
+                                                long long gx) {
   __shared__ float s_den;
-  const int l = blockIdx.y;
   if (threadIdx.x < 32) {
     // No partial sums: a plain FP16 rounding (denominator 1).
-    const float den = partial ? norm_den(partial + static_cast<long long>(l) * chunks, chunks, eps)
+    const float den = partial ? norm_den(partial + l * chunks, chunks, eps)
                               : 1.0f;
     if (threadIdx.x == 0) s_den = den;
   }
   __syncthreads();
   const float den = s_den;
-  const T* xm = x + static_cast<long long>(l) * sL;
-  __half* out = xh + static_cast<long long>(l) * Rp * Cp;
+  const T* xm = x + l * sL;
+  __half* out = xh + l * Rp * Cp;
   if (flat && Rp == R && Cp == C) {
     const long long E = R * C;
-    const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
+    const long long stride = gx * NORM_THREADS;
     long long tail = 0;
     if (is_aligned16(xm) && is_aligned16(out)) {
       // 8 elements per 16-byte store, two groups in flight per thread.
       const long long n8 = E / 8;
-      long long v = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x;
+      long long v = bx * NORM_THREADS + threadIdx.x;
       for (; v + stride < n8; v += 2 * stride) {
         float f0[8], f1[8];
         load8(xm + v * 8, f0);
@@ -277,19 +285,79 @@ __global__ void __launch_bounds__(NORM_THREADS)
       }
       tail = n8 * 8;
     }
-    for (long long e = tail + static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < E;
+    for (long long e = tail + bx * NORM_THREADS + threadIdx.x; e < E;
          e += stride)
       out[e] = __float2half_rn(__fdiv_rn(to_f32(xm[e]), den));
   } else {
     const long long E = Rp * Cp;
-    for (long long e = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < E;
-         e += static_cast<long long>(gridDim.x) * NORM_THREADS) {
+    for (long long e = bx * NORM_THREADS + threadIdx.x; e < E;
+         e += gx * NORM_THREADS) {
       const long long r = e / Cp, c = e - r * Cp;
       float v = 0.f;
       if (r < R && c < C) v = __fdiv_rn(to_f32(xm[r * sR + c * sC]), den);
       out[e] = __float2half_rn(v);
     }
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_scale_cast_kernel(const T* __restrict__ x, long long R, long long C, long long sL,
+                         long long sR, long long sC, int flat, const double* __restrict__ partial,
+                         int chunks, float eps, __half* __restrict__ xh, long long Rp,
+                         long long Cp) {
+  scale_cast_body(x, R, C, sL, sR, sC, flat, partial, chunks, eps, xh, Rp, Cp, blockIdx.y, blockIdx.x,
+                  gridDim.x);
+}
+
+// Both passes over up to NORM_BATCH_MAX problems of one input type, one launch
+// per pass (the normalisations that open a grouped circuit). The 1-D grid is
+// the concatenation of the problems' own grids, problem i owning blocks
+// [b0, b0 + L * per) with `per` blocks per matrix: its chunks in pass 1, its
+// scale-and-cast blocks in pass 2. Each matrix sees exactly the chunking and
+// arithmetic of the single-problem kernels, so the results are bit-identical.
+constexpr int NORM_BATCH_MAX = 8;
+
+struct NormBatchProblem {
+  const void* x;
+  __half* xh;
+  double* partial;
+  long long R, C, sL, sR, sC, Rp, Cp, chunk_elems;
+  long long b0;   // first block of this problem in the launch
+  long long per;  // blocks per matrix
+  int flat, chunks;
+};
+
+struct NormBatch {
+  NormBatchProblem p[NORM_BATCH_MAX];
+  int count;
+  float eps;
+};
+
+__device__ __forceinline__ int norm_batch_problem(const NormBatch& b, long long blk) {
+  int pi = 0;
+  while (pi + 1 < b.count && blk >= b.p[pi + 1].b0) ++pi;
+  return pi;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_norm_partial_batched_kernel(const __grid_constant__ NormBatch b) {
+  const long long blk = blockIdx.x;
+  const NormBatchProblem& q = b.p[norm_batch_problem(b, blk)];
+  const long long local = blk - q.b0;
+  norm_partial_body(static_cast<const T*>(q.x), q.R, q.C, q.sL, q.sR, q.sC, q.flat, q.chunks,
+                    q.chunk_elems, q.partial, local / q.per, local % q.per);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_scale_cast_batched_kernel(const __grid_constant__ NormBatch b) {
+  const long long blk = blockIdx.x;
+  const NormBatchProblem& q = b.p[norm_batch_problem(b, blk)];
+  const long long local = blk - q.b0;
+  scale_cast_body(static_cast<const T*>(q.x), q.R, q.C, q.sL, q.sR, q.sC, q.flat, q.partial, q.chunks,
+                  b.eps, q.xh, q.Rp, q.Cp, local / q.per, local % q.per, q.per);
 }
 
 // y[l] (R x C, contiguous, type T) = xh[l][:R, :C] (FP16, Rp x Cp).

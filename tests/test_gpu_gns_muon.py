@@ -100,7 +100,32 @@ def test_grouped_many_buckets_batched_launches(cuda_device):
     # applies: one variant for all 10 problems -> 2 launches of 8 + 2
     assert prof["gram"]["launches"] == 2 * 2
     assert prof["apply"]["launches"] == 2 * 2
+    # the normalisations: 8 + 2 problems of one input type, two passes each
+    assert prof["normalize"]["launches"] == 2 * 2
     for b, g in zip(banks, grouped):
+        assert torch.equal(g, polar(b))
+
+
+def test_grouped_normalisations_batched_by_type(cuda_device):
+    """The normalisations of a grouped call run as one launch per pass for all
+    problems of one input type; strided, padded and mixed-type banks still
+    equal their own calls bit for bit."""
+    from polar_switch import _native as nat
+    from polar_switch import make_polynomial_orthogonalizer
+    polar = make_polynomial_orthogonalizer("PS3_55")
+    banks = [seeded((2, 128, 256), 81).to(torch.bfloat16), seeded((1, 200, 96), 82).to(torch.bfloat16),
+             seeded((192, 256), 80).t(), seeded((3, 128, 128), 83), seeded((1, 64, 72), 84).half(),
+             seeded((2, 130, 66), 85)]
+    banks = [b.to(cuda_device) for b in banks]
+    assert not banks[2].is_contiguous()
+    nat.profile_enable(True)
+    grouped = polar.grouped(banks)
+    prof = nat.profile_read()
+    nat.profile_enable(False)
+    # bf16 (2 problems), f32 (3) and f16 (1): two passes each
+    assert prof["normalize"]["launches"] == 3 * 2
+    for b, g in zip(banks, grouped):
+        assert g.dtype == b.dtype and g.shape == b.shape
         assert torch.equal(g, polar(b))
 
 
