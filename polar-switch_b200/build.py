@@ -20,7 +20,8 @@ LIB_NAME = "libpolarswitch_b200.so"
 LIB_PATH = os.path.join(LIB_DIR, LIB_NAME)
 HEADER = os.path.join(ROOT, "include", "polar_switch_b200.h")
 SOURCES = [os.path.join(CSRC, "ps_capi.cu")]
-DEPENDS = SOURCES + [os.path.join(CSRC, f) for f in ("ps_ptx.cuh", "ps_gemm.cuh", "ps_norm.cuh")] + [HEADER]
+# Every header under csrc/ is included by ps_capi.cu; a change to any of them rebuilds.
+DEPENDS = SOURCES + sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")) + [HEADER]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

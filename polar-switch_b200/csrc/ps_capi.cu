@@ -274,6 +274,7 @@ ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
   a.a_tri = g.a_tri;
   a.b_tri = g.b_tri;
   a.store_mirror = g.store_mirror;
+  a.same_ab = g.same_ab;
   if (sym) {
     a.tb = (g.M + ps::pair::BM - 1) / ps::pair::BM;
     const int P = (a.tb + 1) / 2;
@@ -543,6 +544,7 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   a.c_bs = n * n;
   a.has_addend = c != nullptr;
   a.has_diag = diag != 0.f;
+  a.same_ab = same ? 1 : 0;  // ta and tb above: same pointer, shape and box
   const double nn = static_cast<double>(n) * n;
   const double bytes = L * nn * 2.0 * ((same ? 1 : 2) + (c ? 1 : 0) + 1);
   if (same && tri) {

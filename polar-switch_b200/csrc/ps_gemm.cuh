@@ -71,6 +71,9 @@ struct GemmArgs {
   // blocks (read through the second maps, see tri_transposed); store_mirror = 0
   // keeps a symmetric result that way (no transposed stores).
   int a_tri, b_tri, store_mirror;
+  // Symmetric A . A^T with both operands read through identical maps: the
+  // CTA-pair kernel then stages a diagonal pair tile's rows once.
+  int same_ab;
   int* status;               // device status word
   long long wait_limit;      // cycles before a bounded wait gives up
 };

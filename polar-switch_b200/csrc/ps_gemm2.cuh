@@ -29,6 +29,13 @@
 // with tcgen05.commit; all 16 epilogue warps release an accumulator on the
 // leader's barrier. Every wait is bounded as in ps_gemm.cuh. Loads fill only
 // the issuing CTA's own shared memory.
+//
+// Diagonal pair tiles of A . A^T (q == p, same_ab): each CTA's half of B is
+// the same 128 rows as its A block, read through an identical map, so the
+// producers load only A, the leader arms the barrier with A's bytes alone and
+// the B descriptor points at the A stage. The UMMAs read the same bytes as
+// with a separate B copy, so the results are unchanged, and these tiles stream
+// half the operand bytes from L2.
 #pragma once
 
 #include "ps_gemm.cuh"
@@ -67,6 +74,7 @@ struct PairArgs {
   int has_addend, has_diag;
   int a_tri, b_tri;       // operand stored as upper-triangle blocks only
   int store_mirror;       // symmetric: also store the transposed off-diagonal blocks
+  int same_ab;            // symmetric A . A^T, A and B maps identical (see below)
   int* status;
   long long wait_limit;
 };
@@ -105,6 +113,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmD, const PairArgs args) {
   // tmA / tmB: boxes in the operand's native majorness (A_MN / B_MN);
   // tmA2 / tmB2: the other majorness, used only for triangle-stored operands.
+  constexpr bool kCanShare = SYM && (A_MN == B_MN);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -171,6 +180,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int nb = n0 + static_cast<int>(rank) * BNH;  // this CTA's half of B
         const int a_lo = (m0 - static_cast<int>(rank) * BM) / BM;  // leader's row block
         const int b_lo = n0 / BM;                                 // leader's B block
+        const bool share = kCanShare && args.same_ab && args.a_tri == args.b_tri && a_lo == b_lo;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status,
                                  kStatusProducerTimeout, args.wait_limit)) {
@@ -180,7 +190,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* a_dst = smem + stage * STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_STAGE_BYTES;
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          if (leader) mbar_arrive_expect_tx(&full[stage], share ? 2 * A_STAGE_BYTES : 2 * STAGE_BYTES);
           const int k0 = kb * BK;
           const bool at = args.a_tri && tri_transposed(A_MN, a_lo, a_lo + 1, k0 / BM);
           const bool bt = args.b_tri && tri_transposed(B_MN, b_lo, b_lo + 1, k0 / BM);
@@ -193,7 +203,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int j = 0; j < BM / 64; ++j)
               tma_load_3d_pair(ma, a_dst + j * MN_ATOM_BYTES, bar, m0 + 64 * j, k0, b);
           }
-          if (B_MN == bt) {
+          if (share) {
+            // B half == A block: nothing more to load
+          } else if (B_MN == bt) {
             tma_load_3d_pair(mb, b_dst, bar, k0, nb, b);
           } else {
 #pragma unroll
@@ -246,6 +258,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int tb_, tm0_, tn0_;
         decode<SYM>(args, t, 0, tb_, tm0_, tn0_);
         const int a_lo = tm0_ / BM, b_lo = tn0_ / BM;
+        const bool share = kCanShare && args.same_ab && args.a_tri == args.b_tri && a_lo == b_lo;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.status, kStatusMmaTimeout,
                                  args.wait_limit)) {
@@ -254,7 +267,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_STAGE_BYTES;
+          const uint32_t b_addr = share ? a_addr : a_addr + A_STAGE_BYTES;
           const int kb128 = (kb * BK) / BM;
           const bool a_mn = A_MN != (args.a_tri && tri_transposed(A_MN, a_lo, a_lo + 1, kb128));
           const bool b_mn = B_MN != (args.b_tri && tri_transposed(B_MN, b_lo, b_lo + 1, kb128));
