@@ -16,6 +16,12 @@ weight decay and the scaled update. Two things differ in how it runs:
     bucket (ps_muon_update) instead of three elementwise passes per matrix.
 
 `parameter_groups` is the reference's grouping (training/muon.py:14-28).
+
+`ShardedMuon` is the same update run across ranks the way the reference's
+NanoGPT optimizer shards its parameter banks (train_nanogpt.py:3983-4037):
+gradients averaged and scattered in chunks of whole matrices, momentum kept
+only for the local chunk, one grouped orthogonalization of all local chunks,
+and the updated chunks gathered back into every rank's banks.
 """
 
 import ctypes
@@ -126,3 +132,113 @@ class Muon(torch.optim.Optimizer):
                     for p, u in zip(params, update.unbind()):
                         p.mul_(1 - group["lr"] * group["weight_decay"])
                         p.add_(u.to(p.dtype), alpha=-group["lr"] * factor)
+
+
+def padded_count(count, world_size):
+    """Matrices a bank holds so that every rank owns the same number: count
+    rounded up to a multiple of world_size, the extra matrices zero (the
+    reference's next_multiple_of_n, train_nanogpt.py:4880-4888)."""
+    return -(-int(count) // int(world_size)) * int(world_size)
+
+
+def check_banks(banks, world_size):
+    """Raise ValueError unless every bank is a contiguous (count, rows, cols)
+    tensor whose count splits evenly over world_size ranks."""
+    for bank in banks:
+        if bank.ndim != 3 or not bank.is_contiguous():
+            raise ValueError("ShardedMuon: each parameter must be a contiguous (count, rows, cols) bank")
+        if bank.shape[0] % world_size:
+            raise ValueError(f"ShardedMuon: a bank of {bank.shape[0]} matrices does not split over "
+                             f"{world_size} ranks; pad it to padded_count()")
+
+
+class ShardedMuon(torch.optim.Optimizer):
+    """Nesterov Muon over parameter banks sharded across ranks.
+
+    Each parameter is a bank of same-shape matrices, shape (count, rows, cols)
+    with count a multiple of the world size (`padded_count`; padding matrices
+    are zero and stay zero). Per step, as the reference's NanoGPT optimizer
+    (train_nanogpt.py:3983-4037, `_launch_reduce` / `_launch_gather`):
+
+      1. every bank's gradient is averaged over ranks and scattered, rank r
+         receiving matrices [r * chunk, (r + 1) * chunk) (reduce_scatter_tensor,
+         AVG; all banks' scatters are in flight before the first is used);
+      2. the momentum of the local chunk is updated and its Nesterov direction
+         formed (ps_muon_direction, one kernel per bank; BF16 directions for
+         the "rms" scale);
+      3. the local chunks of all banks are orthogonalized in one grouped call;
+      4. the local slice of every bank gets the decoupled weight decay and the
+         scaled update (ps_muon_update), and all_gather_into_tensor writes every
+         rank's slice into every rank's bank, each gather issued as soon as its
+         slice is updated.
+
+    The update rule and its rounding are those of `Muon` (training/muon.py:
+    54-86), so at world size 1 the two optimizers give the same bits. Runs on
+    CUDA banks (NCCL between ranks); with no process group it is world size 1.
+    """
+
+    def __init__(self, banks, orthogonalize, lr, momentum=0.95, weight_decay=0.0, scale="rms",
+                 group=None):
+        banks = list(banks)
+        super().__init__(banks, dict(lr=lr, momentum=momentum, weight_decay=weight_decay, scale=scale))
+        self.orthogonalize = orthogonalize
+        self.group = group
+        if torch.distributed.is_available() and torch.distributed.is_initialized():
+            self.world_size = torch.distributed.get_world_size(group)
+            self.rank = torch.distributed.get_rank(group)
+        else:
+            self.world_size, self.rank = 1, 0
+        check_banks([b for g in self.param_groups for b in g["params"]], self.world_size)
+
+    def _chunk(self, bank):
+        n = bank.shape[0] // self.world_size
+        return n, bank[self.rank * n:(self.rank + 1) * n]
+
+    def _directions(self, grad_chunk, mom_chunk, momentum, out_dtype):
+        return muon_directions(list(grad_chunk.unbind(0)), list(mom_chunk.unbind(0)), momentum, out_dtype)
+
+    def _update(self, param_chunk, update, decay, alpha):
+        muon_update(list(param_chunk.unbind(0)), update, decay, alpha)
+
+    @torch.no_grad()
+    def step(self):
+        """One optimizer step from the banks' (unreduced, per-rank) gradients."""
+        dist = torch.distributed
+        W = self.world_size
+        entries = []  # (group, bank, local gradient chunk, pending scatter)
+        for g in self.param_groups:
+            for bank in g["params"]:
+                if bank.grad is None:
+                    continue
+                grad = bank.grad.contiguous()
+                n, _ = self._chunk(bank)
+                if W == 1:
+                    entries.append((g, bank, grad, None))
+                    continue
+                local = torch.empty((n, *grad.shape[1:]), device=grad.device, dtype=grad.dtype)
+                work = dist.reduce_scatter_tensor(local, grad, op=dist.ReduceOp.AVG, group=self.group,
+                                                  async_op=True)
+                entries.append((g, bank, local, work))
+        if not entries:
+            return
+        directions = []
+        for g, bank, local, work in entries:
+            if work is not None:
+                work.wait()
+            state = self.state[bank]
+            if "momentum_chunk" not in state:
+                state["momentum_chunk"] = torch.zeros_like(local)
+            out_dtype = torch.bfloat16 if g["scale"] == "rms" else bank.dtype
+            directions.append(self._directions(local, state["momentum_chunk"], g["momentum"], out_dtype))
+        grouped = getattr(self.orthogonalize, "grouped", None)
+        updates = grouped(directions) if grouped is not None else [self.orthogonalize(d) for d in directions]
+        gathers = []
+        for (g, bank, _, _), update in zip(entries, updates):
+            rows, cols = bank.shape[-2:]
+            factor = (0.2 * math.sqrt(max(rows, cols)) if g["scale"] == "rms" else math.sqrt(rows / cols))
+            _, mine = self._chunk(bank)
+            self._update(mine, update.contiguous(), 1 - g["lr"] * g["weight_decay"], -g["lr"] * factor)
+            if W > 1:
+                gathers.append(dist.all_gather_into_tensor(bank.data, mine, group=self.group, async_op=True))
+        for work in gathers:
+            work.wait()

@@ -89,3 +89,32 @@ def test_optimizer_steps_follow_the_reference_rule(cuda_device):
             _reference_step(ref_params[lo:hi], grads[lo:hi], ref_moms[lo:hi], polar, 0.02, 0.95, 0.1)
     for p, r in zip(params, ref_params):
         assert float((p.detach() - r).norm() / r.norm()) < 1e-3
+
+
+def test_sharded_muon_world1_equals_muon(cuda_device):
+    """ShardedMuon on banks at world size 1 runs the same kernels on the same
+    matrices as Muon on the banks' matrices as separate parameters: the same
+    bits after two steps, padding matrices included (they stay zero)."""
+    from polar_switch.muon import ShardedMuon
+    shapes = [(3, 256, 128), (4, 128, 384), (2, 192, 192)]
+    banks = [seeded(s, 500 + i).to(cuda_device) * 0.05 for i, s in enumerate(shapes)]
+    banks[1][3:] = 0  # one padding matrix
+    sharded = [torch.nn.Parameter(b.clone()) for b in banks]
+    single = [torch.nn.Parameter(m.clone()) for b in banks for m in b.unbind(0)]
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    opt_s = ShardedMuon(sharded, polar, lr=0.02, momentum=0.95, weight_decay=0.1)
+    opt_m = Muon([{"params": single, "role": "all"}], polar, lr=0.02, momentum=0.95, weight_decay=0.1)
+    assert opt_s.world_size == 1
+    for step in range(2):
+        grads = [seeded(s, 600 + 10 * step + i).to(cuda_device) for i, s in enumerate(shapes)]
+        grads[1][3:] = 0
+        for p, g in zip(sharded, grads):
+            p.grad = g.clone()
+        for p, g in zip(single, [m for g in grads for m in g.unbind(0)]):
+            p.grad = g.clone()
+        opt_s.step()
+        opt_m.step()
+    flat = [m for b in sharded for m in b.detach().unbind(0)]
+    for a, b in zip(flat, single):
+        assert torch.equal(a, b.detach())
+    assert not sharded[1][3:].any()
