@@ -29,6 +29,7 @@
  *   training/muon.py:59-86 (buckets of one step) -> ps_circuit_grouped
  *   training/muon.py:63-74 momentum/Nesterov/stack/cast -> ps_muon_direction
  *   training/muon.py:84-86 decay and scaled update     -> ps_muon_update
+ *   training/diagnostics.py:161-165 NaN / inf counts, max |x| -> ps_update_stats
  *   (no single counterpart) split-matrix pieces -> ps_sumsq, ps_scale_cast, ps_gram_f32
  */
 #ifndef POLAR_SWITCH_B200_H
@@ -278,6 +279,16 @@ PS_API int ps_muon_direction(const void* const* grads, void* const* moms, int co
 PS_API int ps_muon_update(void* const* params, int count, int64_t elems, int dtype,
                           const void* updates, int upd_dtype, float decay, float alpha,
                           void* stream);
+
+/* Telemetry of orthogonalized updates (replaces the three passes of
+ * training/diagnostics.py:161-165, NormLog.record): for each of L matrices of
+ * `elems` contiguous elements of x_dtype (FP16, BF16 or FP32), in one pass,
+ *   nan_count[l] = number of NaN entries, inf_count[l] = number of infinite
+ *   entries, max_abs[l] = max |x| over the entries that are not NaN
+ *   (infinity if any entry is infinite, 0 if every entry is NaN).
+ * The three outputs are device arrays of L elements, overwritten. */
+PS_API int ps_update_stats(const void* x, int x_dtype, int64_t L, int64_t elems, int64_t* nan_count,
+                           int64_t* inf_count, float* max_abs, void* stream);
 
 #ifdef __cplusplus
 }

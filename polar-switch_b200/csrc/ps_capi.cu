@@ -22,6 +22,7 @@
 #include "ps_gemm2.cuh"
 #include "ps_norm.cuh"
 #include "ps_muon.cuh"
+#include "ps_stats.cuh"
 
 namespace ps {
 // First error code recorded by a bounded wait in any kernel on this device.
@@ -1112,6 +1113,34 @@ int muon_update_in(int upd_dtype, void* const* params, int count, int64_t E, flo
   }
 }
 
+// NaN / infinity counts and max |x| per matrix, matrices of E contiguous
+// elements; outputs zeroed here, on the stream, before the kernel.
+template <typename T>
+int launch_update_stats(const void* x, int64_t L, int64_t E, int64_t* nan_count, int64_t* inf_count,
+                        float* max_abs, int sms, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(nan_count, 0, L * sizeof(int64_t), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(inf_count, 0, L * sizeof(int64_t), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(max_abs, 0, L * sizeof(float), s);
+  if (e != cudaSuccess) return cuda_fail(e, "update stats memset");
+  const int64_t per_mat = (E + ps::NORM_THREADS * 8 - 1) / (ps::NORM_THREADS * 8);
+  for (int64_t l0 = 0; l0 < L; l0 += 65535) {  // grid y is at most 65535
+    const int64_t n = L - l0 < 65535 ? L - l0 : 65535;
+    int64_t gx = (4LL * sms + n - 1) / n;
+    if (gx > per_mat) gx = per_mat;
+    if (gx < 1) gx = 1;
+    LaunchScope scope(kProfOther, s, 0.0, static_cast<double>(n) * E * sizeof(T));
+    ps::ps_update_stats_kernel<T><<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(n)),
+                                    ps::NORM_THREADS, 0, s>>>(
+        static_cast<const T*>(x) + l0 * E, E,
+        reinterpret_cast<unsigned long long*>(nan_count + l0),
+        reinterpret_cast<unsigned long long*>(inf_count + l0),
+        reinterpret_cast<unsigned int*>(max_abs + l0));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "update stats launch");
+  }
+  return PS_OK;
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1368,6 +1397,26 @@ int ps_muon_update(void* const* params, int count, int64_t elems, int dtype, con
       return muon_update_in<__nv_bfloat16>(upd_dtype, params, count, elems, decay, alpha, updates, st->sms, s);
     default:
       return muon_update_in<__half>(upd_dtype, params, count, elems, decay, alpha, updates, st->sms, s);
+  }
+}
+
+int ps_update_stats(const void* x, int x_dtype, int64_t L, int64_t elems, int64_t* nan_count,
+                    int64_t* inf_count, float* max_abs, void* stream) {
+  if (!x || !nan_count || !inf_count || !max_abs) return fail(PS_ERR_INVALID, "ps_update_stats: null pointer");
+  if (L < 1 || elems < 1) return fail(PS_ERR_INVALID, "ps_update_stats: empty input");
+  if (x_dtype != PS_F16 && x_dtype != PS_BF16 && x_dtype != PS_F32)
+    return fail(PS_ERR_INVALID, "ps_update_stats: updates must be FP16, BF16 or FP32");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (x_dtype) {
+    case PS_F16:
+      return launch_update_stats<__half>(x, L, elems, nan_count, inf_count, max_abs, st->sms, s);
+    case PS_BF16:
+      return launch_update_stats<__nv_bfloat16>(x, L, elems, nan_count, inf_count, max_abs, st->sms, s);
+    default:
+      return launch_update_stats<float>(x, L, elems, nan_count, inf_count, max_abs, st->sms, s);
   }
 }
 

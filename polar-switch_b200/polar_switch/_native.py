@@ -30,7 +30,7 @@ EXPORTED = (
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
     "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
-    "ps_gram_f32", "ps_muon_direction", "ps_muon_update",
+    "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
 )
 
 
@@ -94,6 +94,7 @@ _SIGNATURES = {
     "ps_muon_direction": ([ctypes.POINTER(_ptr), ctypes.POINTER(_ptr), _int, _i64, _int, _f32, _int, _ptr,
                            _int, _ptr], _int),
     "ps_muon_update": ([ctypes.POINTER(_ptr), _int, _i64, _int, _ptr, _int, _f32, _f32, _ptr], _int),
+    "ps_update_stats": ([_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _ptr], _int),
     "ps_gns": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _int, _int, ctypes.POINTER(_f32),
                 _int, ctypes.POINTER(ctypes.c_int32), _f32, _ptr, _i64, _ptr], _int),
     "ps_profile_enable": ([_int], _int),

@@ -218,3 +218,28 @@ def gram_f32(X, out=None):
         nat.check("ps_gram_f32", nat.load().ps_gram_f32(nat.ptr(X), nat.ptr(out), L, rows, cols, cols,
                                                         nat.stream_ptr(X.device)))
     return out
+
+
+def update_stats(X):
+    """Per matrix of X (..., rows, cols): (NaN count, infinite count, max |x|)
+    as int64, int64 and float32 tensors of shape X.shape[:-2], from one pass
+    over X (ps_update_stats). Like torch's abs().amax(), max |x| is NaN for a
+    matrix with a NaN entry and infinite for one with an infinite entry."""
+    if not isinstance(X, torch.Tensor) or not X.is_cuda:
+        raise NotImplementedError("update_stats: polar_switch_b200 runs on CUDA tensors only")
+    if X.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise TypeError(f"update_stats: expected FP16, BF16 or FP32, got {X.dtype}")
+    if X.ndim < 2 or X.numel() == 0:
+        raise ValueError("update_stats: expected nonempty matrices")
+    W = _batched(X.contiguous())
+    L = W.shape[0]
+    nan = torch.empty(L, device=X.device, dtype=torch.int64)
+    inf = torch.empty(L, device=X.device, dtype=torch.int64)
+    amax = torch.empty(L, device=X.device, dtype=torch.float32)
+    with torch.cuda.device(X.device):
+        nat.check("ps_update_stats", nat.load().ps_update_stats(
+            nat.ptr(W), nat.DTYPE_CODES[X.dtype], L, W.shape[1] * W.shape[2], nat.ptr(nan), nat.ptr(inf),
+            nat.ptr(amax), nat.stream_ptr(X.device)))
+    amax = torch.where(nan > 0, torch.full_like(amax, float("nan")), amax)
+    shape = X.shape[:-2]
+    return nan.reshape(shape), inf.reshape(shape), amax.reshape(shape)

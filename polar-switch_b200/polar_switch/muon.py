@@ -172,17 +172,23 @@ class ShardedMuon(torch.optim.Optimizer):
          rank's slice into every rank's bank, each gather issued as soon as its
          slice is updated.
 
+    With a `norm_log` (polar_switch.diagnostics.NormLog) every local chunk's
+    orthogonalized update is recorded before it is applied, labelled with the
+    bank's `label` attribute (else its group's "role") and starting at matrix
+    rank * chunk, as train_nanogpt.py:4276-4278 records it.
+
     The update rule and its rounding are those of `Muon` (training/muon.py:
     54-86), so at world size 1 the two optimizers give the same bits. Runs on
     CUDA banks (NCCL between ranks); with no process group it is world size 1.
     """
 
     def __init__(self, banks, orthogonalize, lr, momentum=0.95, weight_decay=0.0, scale="rms",
-                 group=None):
+                 group=None, norm_log=None):
         banks = list(banks)
         super().__init__(banks, dict(lr=lr, momentum=momentum, weight_decay=weight_decay, scale=scale))
         self.orthogonalize = orthogonalize
         self.group = group
+        self.norm_log = norm_log
         if torch.distributed.is_available() and torch.distributed.is_initialized():
             self.world_size = torch.distributed.get_world_size(group)
             self.rank = torch.distributed.get_rank(group)
@@ -233,7 +239,11 @@ class ShardedMuon(torch.optim.Optimizer):
         grouped = getattr(self.orthogonalize, "grouped", None)
         updates = grouped(directions) if grouped is not None else [self.orthogonalize(d) for d in directions]
         gathers = []
-        for (g, bank, _, _), update in zip(entries, updates):
+        for i, ((g, bank, _, _), update) in enumerate(zip(entries, updates)):
+            if self.norm_log is not None:
+                label = getattr(bank, "label", None) or g.get("role") or f"bank{i}"
+                self.norm_log.record(label, update, self.rank * (bank.shape[0] // W),
+                                     execution=getattr(self.orthogonalize, "last_execution", None))
             rows, cols = bank.shape[-2:]
             factor = (0.2 * math.sqrt(max(rows, cols)) if g["scale"] == "rms" else math.sqrt(rows / cols))
             _, mine = self._chunk(bank)

@@ -49,6 +49,16 @@ class _CpuShardedMuon(ShardedMuon):
         _update(param_chunk, update, decay, alpha)
 
 
+class _RecordingLog:
+    """Stands in for NormLog: keeps (label, shape, matrix_start) per record."""
+
+    def __init__(self):
+        self.calls = []
+
+    def record(self, label, output, matrix_start=0, execution=None, matrix_names=None):
+        self.calls.append((label, tuple(output.shape), matrix_start))
+
+
 def _banks(shapes, padding):
     g = torch.Generator().manual_seed(11)
     banks = []
@@ -82,8 +92,9 @@ def _worker(rank, world, port, shapes, padding, steps, scale, q):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
         banks = [torch.nn.Parameter(b) for b in _banks(shapes, padding)]
+        log = _RecordingLog()
         opt = _CpuShardedMuon(banks, _orthogonalize, lr=LR, momentum=MOMENTUM, weight_decay=DECAY,
-                              scale=scale)
+                              scale=scale, norm_log=log)
         assert (opt.world_size, opt.rank) == (world, rank)
         for step in range(steps):
             for b, gr in zip(banks, _grads(shapes, padding, rank, step)):
@@ -92,6 +103,9 @@ def _worker(rank, world, port, shapes, padding, steps, scale, q):
         # numpy, not tensors: a tensor would travel as a shared-memory handle
         # that dies with this process
         moms = [opt.state[b]["momentum_chunk"].numpy().copy() for b in banks]
+        n = [s[0] // world for s in shapes]
+        assert log.calls == [(f"bank{i}", (n[i], *shapes[i][1:]), rank * n[i])
+                             for _ in range(steps) for i in range(len(shapes))], log.calls
         q.put((rank, ([b.detach().numpy().copy() for b in banks], moms)))
         dist.barrier()
         dist.destroy_process_group()
