@@ -536,7 +536,9 @@ def main():
                                         "bucket_matrices": [sum(c for _, _, c in p["pieces"]) for p in step.plans],
                                         "bytes_per_step": step.recv.numel() * 2}
         if args.workload == "single":
-            line["vs_baseline"] = value / 1177.0  # published 7.47 ms for 8192^2 PS2-55
+            # the reference's published 7.47 ms for one 8192 x 8192 PS2-55 call on a B200
+            # (README.md:77-81, figures/fp16_timing_heatmaps.png): 16 * 8192^3 / 7.47 ms = 1177 TFLOP/s
+            line["vs_baseline"] = value / 1177.0
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.cuda.synchronize(device)
