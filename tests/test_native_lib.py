@@ -51,6 +51,12 @@ def test_invalid_arguments_are_rejected_before_any_device_work():
     assert b"square" in lib.ps_last_error()
     assert lib.ps_gns(ws, 1, 1, 8, 16, 128, 16, 1, ws, 1, 0, coeffs, 0, resets, 1e-7, ws, 1 << 20,
                       null) == _native.PS_ERR_INVALID
+    # ps_update_stats: null outputs, an empty batch and FP64 (not an update type) are argument errors
+    assert lib.ps_update_stats(ws, _native.PS_F16, 2, 64, null, ws, ws, null) == _native.PS_ERR_INVALID
+    assert b"null" in lib.ps_last_error()
+    assert lib.ps_update_stats(ws, _native.PS_F16, 0, 64, ws, ws, ws, null) == _native.PS_ERR_INVALID
+    assert lib.ps_update_stats(ws, _native.PS_F64, 2, 64, ws, ws, ws, null) == _native.PS_ERR_INVALID
+    assert b"FP16, BF16 or FP32" in lib.ps_last_error()
 
 
 def test_struct_layouts_match_header():
