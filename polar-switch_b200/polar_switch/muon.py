@@ -180,6 +180,11 @@ class ShardedMuon(torch.optim.Optimizer):
     The update rule and its rounding are those of `Muon` (training/muon.py:
     54-86), so at world size 1 the two optimizers give the same bits. Runs on
     CUDA banks (NCCL between ranks); with no process group it is world size 1.
+    The collectives pair up bank by bank in parameter order, so every rank
+    must hold gradients for the same banks, as data-parallel training gives
+    (a bank with no gradient on any rank is skipped by all). Checking this
+    at run time would cost a host synchronisation per step, so it is not
+    checked.
     """
 
     def __init__(self, banks, orthogonalize, lr, momentum=0.95, weight_decay=0.0, scale="rms",
