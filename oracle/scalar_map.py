@@ -25,6 +25,23 @@ def circuit_map(table, x):
     return x
 
 
+def circuit_map_stored(table, x, factor):
+    """circuit_map with every stored value multiplied by factor(shape): the
+    Gram, each inner iteration's buffer and each outer iteration's output.
+    This is the rounding model under which the reference certified its
+    circuits' upper endpoints (coefficient_search/stage*.json "verification":
+    every stored value times a factor in [1/safety, safety])."""
+    x = np.asarray(x, dtype=np.float64)
+    for residual, steps in table:
+        B = {0: x * x * factor(x.shape)}
+        last = 0
+        for w, i, r, a, b, c in steps:
+            B[w] = (a * B[i] * B[i] + b * B[r] + c) * factor(x.shape)
+            last = w
+        x = (B[last] * x + residual * x) * factor(x.shape)
+    return x
+
+
 def quintic_map(coefficients, x):
     """Compose quintics x <- a x + b x^3 + c x^5 (Gram Newton-Schulz steps)."""
     x = np.asarray(x, dtype=np.float64)

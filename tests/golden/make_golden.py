@@ -4,7 +4,8 @@ Run in the build container, where the reference project is available:
 
     python tests/golden/make_golden.py --reference /path/to/polar-switch
 
-It imports the reference package and runs its own code on CPU:
+It reads the reference's certified circuits (coefficient_search/stage*.json)
+and imports the reference package to run its own code on CPU:
   * the Triton backend (polar_switch/triton_kernels.py) under
     TRITON_INTERPRET=1 -- the kernel the reference uses whenever QuACK does
     not apply, evaluated by Triton's CPU interpreter;
@@ -29,10 +30,41 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
+def certified(reference):
+    """certified_circuits.json: the two circuits the reference certified with
+    interval arithmetic (coefficient_search/stage1.json, stage2.json; PS2-64's
+    outer iterations), as coefficient-table steps (w, i, r, a, b, c) with the
+    buffers A = 0 and B = 1, and their certified intervals."""
+    import json
+    buf = {"A": 0, "B": 1}
+    out = {}
+    for stage in ("stage1", "stage2"):
+        with open(os.path.join(reference, "coefficient_search", stage + ".json")) as f:
+            d = json.load(f)
+        assert d["status"] == "verified" and d["format"] == "two-buffer-iteration-v2"
+        out[stage] = {
+            "input_interval": d["input_interval"],
+            "output_interval": d["output_interval"],
+            "exact_intervals": d["exact_intervals"],
+            "safety_factor": d["safety_factor"],
+            "centered": d["centered"],
+            "steps": [[buf[s["write"]], buf[s["square"]], buf[s["addend"]], s["a"], s["b"], s["c"]]
+                      for s in d["iteration"]["steps"]],
+        }
+    with open(os.path.join(HERE, "certified_circuits.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    print("wrote certified_circuits.json")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference project")
+    ap.add_argument("--only", choices=["all", "certified"], default="all",
+                    help="'certified' writes certified_circuits.json alone")
     args = ap.parse_args()
+    certified(os.path.abspath(args.reference))
+    if args.only == "certified":
+        return
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, os.path.abspath(args.reference))
     import torch

@@ -7,6 +7,10 @@
   * GNS against the reference's PyTorch recurrence.
   * Scalar maps of every table against the published final intervals
     (reference README.md:64-73, polar_switch/README.md:31-44).
+  * The two circuits the reference certified by interval arithmetic
+    (coefficient_search/stage1.json, stage2.json; PS2-64's outer iterations)
+    against their certified intervals, exactly and under the certification's
+    rounding model, and the PS2_64 table against them.
 """
 
 import json
@@ -112,6 +116,75 @@ def test_scalar_map_published_interval(method):
     lo, hi = sm.final_interval(lambda x: sm.circuit_map(table, x))
     plo, phi = PUBLISHED[method]
     assert abs(lo - plo) < 2e-6 and abs(hi - phi) < 2e-6, (method, lo, hi)
+
+
+def _certified():
+    with open(os.path.join(GOLDEN, "certified_circuits.json")) as f:
+        data = json.load(f)
+    for c in data.values():
+        c["table"] = ((0.0, tuple(tuple(st) for st in c["steps"])),)
+    return data
+
+
+def test_certified_intervals_are_the_exact_rationals():
+    from fractions import Fraction
+    for c in _certified().values():
+        for key, exact in (("input_interval", "input"), ("output_interval", "output")):
+            assert [float(Fraction(v)) for v in c["exact_intervals"][exact]] == c[key]
+        assert Fraction(c["safety_factor"]) == Fraction(201, 200)
+
+
+@pytest.mark.parametrize("stage", ["stage1", "stage2"])
+def test_certified_circuit_exact_map(stage):
+    """The exact circuit maps its input interval into the certified output
+    interval, and its minimum is the certified lower endpoint (tight to the
+    certification's tolerance)."""
+    c = _certified()[stage]
+    lo, hi = c["input_interval"]
+    out_lo, out_hi = c["output_interval"]
+    y_lo, y_hi = sm.final_interval(lambda x: sm.circuit_map(c["table"], x), lo, hi)
+    assert out_lo <= y_lo <= out_lo + 1e-10, (y_lo, out_lo)
+    assert y_hi <= out_hi
+
+
+@pytest.mark.parametrize("stage", ["stage1", "stage2"])
+def test_certified_circuit_upper_endpoint_under_rounding(stage):
+    """With every stored value multiplied by a random factor in
+    [1/safety, safety] (the certification's rounding model), the output never
+    exceeds the certified upper endpoint."""
+    c = _certified()[stage]
+    lo, hi = c["input_interval"]
+    s = 201 / 200
+    rng = np.random.default_rng(17)
+    x = np.exp(np.linspace(np.log(lo), np.log(hi), 100_001))
+    worst = -np.inf
+    for _ in range(20):
+        y = sm.circuit_map_stored(c["table"], x, lambda shape: rng.uniform(1 / s, s, size=shape))
+        worst = max(worst, float(y.max()))
+        # the extreme factors, all at once, on every stored value
+        for f in (s, 1 / s):
+            y = sm.circuit_map_stored(c["table"], x, lambda shape, f=f: np.full(shape, f))
+            worst = max(worst, float(y.max()))
+    assert worst <= c["output_interval"][1], worst
+
+
+def test_ps2_64_table_matches_the_certified_circuits():
+    """coefficients.PS2_64 is the certified pair of circuits up to ~1e-7 in the
+    coefficients: same buffer structure, each outer iteration's interval
+    within 2e-8 of the certified lower endpoint and under the upper one, and
+    the composition gives the published PS2-64 interval."""
+    cert = _certified()
+    for k, stage in enumerate(("stage1", "stage2")):
+        c = cert[stage]
+        ours = coefficients.PS2_64[k]
+        assert ours[0] == 0 and [st[:3] for st in ours[1]] == [st[:3] for st in c["table"][0][1]]
+        for a, b in zip(ours[1], c["table"][0][1]):
+            assert np.allclose(a[3:], b[3:], rtol=1e-7, atol=0)
+        lo, hi = c["input_interval"]
+        y_lo, y_hi = sm.final_interval(lambda x: sm.circuit_map((ours,), x), lo, hi)
+        assert abs(y_lo - c["output_interval"][0]) <= 2e-8 and y_hi <= c["output_interval"][1]
+    y_lo, y_hi = sm.final_interval(lambda x: sm.circuit_map(coefficients.PS2_64, x))
+    assert abs(y_lo - 0.8971109) < 1e-7 and abs(y_hi - 1.0812121) < 1e-7
 
 
 def test_gns_scalar_map_published_interval():
