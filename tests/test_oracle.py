@@ -210,3 +210,16 @@ def test_oracle_noise_floor_is_small_on_gaussian_inputs():
     a = oc.run_circuit(X, coefficients.PS2_55, acc=torch.float32)
     b = oc.run_circuit(X, coefficients.PS2_55, acc=torch.float64)
     assert oc.relative_frobenius(a, b) < 2e-3
+
+
+@pytest.mark.parametrize("method,interval", [("PS2_55", (0.87219, 1.10286)), ("PS3_55", (0.89809, 1.08094))])
+def test_config1_singular_interval_known_answer(method, interval):
+    """BASELINE config 1 (N(0,1) 1024 x 2048, torch CPU generator seed 0):
+    the singular-value interval of the circuit's output as recorded, to five
+    decimals, by an independent FP32-accumulation emulation of the reference
+    when the configurations were written down. Agreement to 3e-5 (FP16 output
+    rounding in either emulation moves the extremes by ~1e-5)."""
+    X = torch.randn(1024, 2048, generator=torch.Generator().manual_seed(0))
+    Y = oc.run_circuit(X, getattr(coefficients, method), acc=torch.float32)
+    s = torch.linalg.svdvals(Y.double())
+    assert abs(float(s.min()) - interval[0]) <= 3e-5 and abs(float(s.max()) - interval[1]) <= 3e-5
