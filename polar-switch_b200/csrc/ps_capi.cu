@@ -706,6 +706,10 @@ int64_t norm_partials_per_matrix(int64_t L, int64_t rows, int64_t cols, int sms)
   return a > b ? a : b;
 }
 
+// Largest grid y extent; launches that put matrices on grid y cover longer
+// batches in slices of this many matrices.
+constexpr int64_t kMaxGridY = 65535;
+
 // Pass 1: chunk sums of squares. Contiguous input is summed over chunks of
 // `chunk_elems` elements, strided input over `chunks` row ranges; returns the
 // number of chunk sums per matrix through `chunks_out`.
@@ -716,12 +720,17 @@ int launch_norm_pass1(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL
   const int flat = (sC == 1 && sR == C) ? 1 : 0;
   if (flat) chunks = static_cast<int>((R * C + chunk_elems - 1) / chunk_elems);
   *chunks_out = chunks;
-  dim3 g1(chunks, static_cast<unsigned>(L));
-  LaunchScope scope(kProfNormalize, s, 2.0 * L * R * C, static_cast<double>(L) * R * C * sizeof(T));
-  ps::ps_norm_partial_kernel<T><<<g1, ps::NORM_THREADS, 0, s>>>(
-      static_cast<const T*>(x), R, C, sL, sR, sC, flat, chunks, chunk_elems, partial);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? PS_OK : cuda_fail(e, "normalize launch (pass 1)");
+  for (int64_t l0 = 0; l0 < L; l0 += kMaxGridY) {  // matrices run along grid y
+    const int64_t n = L - l0 < kMaxGridY ? L - l0 : kMaxGridY;
+    dim3 g1(chunks, static_cast<unsigned>(n));
+    LaunchScope scope(kProfNormalize, s, 2.0 * n * R * C, static_cast<double>(n) * R * C * sizeof(T));
+    ps::ps_norm_partial_kernel<T><<<g1, ps::NORM_THREADS, 0, s>>>(
+        static_cast<const T*>(x) + l0 * sL, R, C, sL, sR, sC, flat, chunks, chunk_elems,
+        partial + l0 * chunks);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 1)");
+  }
+  return PS_OK;
 }
 
 // Pass 2: xh = fp16(x / den) with den from `chunks` sums per matrix (partial
@@ -735,14 +744,19 @@ int launch_norm_pass2(const void* x, int64_t L, int64_t R, int64_t C, int64_t sL
   int64_t gx = (4LL * sms + L - 1) / L;
   if (gx > per_mat_blocks) gx = per_mat_blocks;
   if (gx < 1) gx = 1;
-  dim3 g2(static_cast<unsigned>(gx), static_cast<unsigned>(L));
-  LaunchScope scope(kProfNormalize, s, static_cast<double>(L) * R * C,
-                    static_cast<double>(L) * R * C * sizeof(T) + 2.0 * L * Rp * Cp);
-  ps::ps_scale_cast_kernel<T><<<g2, ps::NORM_THREADS, 0, s>>>(
-      static_cast<const T*>(x), R, C, sL, sR, sC, flat, partial, chunks, eps,
-      static_cast<__half*>(xh), Rp, Cp);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? PS_OK : cuda_fail(e, "normalize launch (pass 2)");
+  for (int64_t l0 = 0; l0 < L; l0 += kMaxGridY) {  // matrices run along grid y
+    const int64_t n = L - l0 < kMaxGridY ? L - l0 : kMaxGridY;
+    dim3 g2(static_cast<unsigned>(gx), static_cast<unsigned>(n));
+    LaunchScope scope(kProfNormalize, s, static_cast<double>(n) * R * C,
+                      static_cast<double>(n) * R * C * sizeof(T) + 2.0 * n * Rp * Cp);
+    ps::ps_scale_cast_kernel<T><<<g2, ps::NORM_THREADS, 0, s>>>(
+        static_cast<const T*>(x) + l0 * sL, R, C, sL, sR, sC, flat,
+        partial ? partial + l0 * chunks : nullptr, chunks, eps,
+        static_cast<__half*>(xh) + l0 * Rp * Cp, Rp, Cp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "normalize launch (pass 2)");
+  }
+  return PS_OK;
 }
 
 // Two passes.
@@ -1123,8 +1137,8 @@ int launch_update_stats(const void* x, int64_t L, int64_t E, int64_t* nan_count,
   if (e == cudaSuccess) e = cudaMemsetAsync(max_abs, 0, L * sizeof(float), s);
   if (e != cudaSuccess) return cuda_fail(e, "update stats memset");
   const int64_t per_mat = (E + ps::NORM_THREADS * 8 - 1) / (ps::NORM_THREADS * 8);
-  for (int64_t l0 = 0; l0 < L; l0 += 65535) {  // grid y is at most 65535
-    const int64_t n = L - l0 < 65535 ? L - l0 : 65535;
+  for (int64_t l0 = 0; l0 < L; l0 += kMaxGridY) {  // matrices run along grid y
+    const int64_t n = L - l0 < kMaxGridY ? L - l0 : kMaxGridY;
     int64_t gx = (4LL * sms + n - 1) / n;
     if (gx > per_mat) gx = per_mat;
     if (gx < 1) gx = 1;
