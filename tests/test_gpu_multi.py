@@ -1,7 +1,10 @@
 """The sharded Muon step on 2 GPUs (one process per GPU, NCCL): both gather
 transports (copy-engine pushes into symmetric memory, and the NCCL
 all-gather) must give every rank exactly the updates a single process
-computes for the same banks. Skipped with fewer than two GPUs."""
+computes for the same banks; a matrix split across the two GPUs must stay
+within the circuit's tolerance; and the whole bank-sharded optimizer step
+(ShardedMuon) must give every rank the banks one process computes. Skipped
+with fewer than two GPUs."""
 
 import os
 import socket
@@ -162,3 +165,83 @@ def test_two_gpu_split_matrix_matches_the_circuit(cuda_device):
         err = oc.relative_frobenius(split, ref64)
         assert err <= max(5e-3, 2.0 * floor, 1.25 * err_whole), (err, err_whole, floor)
         assert oc.relative_frobenius(split, whole) <= 1e-2
+
+
+MUON_SHAPES = [(4, 256, 128), (2, 128, 384)]
+
+
+def _grad(shape, step, rank, i):
+    """A rank's gradient: multiples of 1/16, so the average over ranks is exact."""
+    g = torch.Generator().manual_seed(100 * step + 10 * rank + i)
+    return torch.randint(-64, 65, shape, generator=g).float() / 16
+
+
+def _muon_worker(rank, world, port, q):
+    try:
+        import datetime
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [os.path.join(root, "polar-switch_b200"), root]
+        import torch.distributed as dist
+        from polar_switch import make_polynomial_orthogonalizer
+        from polar_switch.muon import Muon, ShardedMuon
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        g = torch.Generator().manual_seed(21)
+        init = [torch.randn(*s, generator=g) * 0.05 for s in MUON_SHAPES]
+        polar = make_polynomial_orthogonalizer("PS2_55")
+        banks = [torch.nn.Parameter(b.to(dev)) for b in init]
+        opt = ShardedMuon(banks, polar, lr=0.02, momentum=0.95, weight_decay=0.1)
+        for step in range(2):
+            for i, (b, s) in enumerate(zip(banks, MUON_SHAPES)):
+                b.grad = _grad(s, step, rank, i).to(dev)
+            opt.step()
+        torch.cuda.synchronize()
+        # one process, this GPU: Muon on the same matrices with the averaged gradients
+        single = [torch.nn.Parameter(m.clone().to(dev)) for b in init for m in b.unbind(0)]
+        ref = Muon([{"params": single, "role": "all"}], polar, lr=0.02, momentum=0.95, weight_decay=0.1)
+        for step in range(2):
+            avg = [sum(_grad(s, step, r, i) for r in range(world)) / world for i, s in enumerate(MUON_SHAPES)]
+            for p, x in zip(single, [m for a in avg for m in a.unbind(0)]):
+                p.grad = x.to(dev)
+            ref.step()
+        torch.cuda.synchronize()
+        flat = [m for b in banks for m in b.detach().unbind(0)]
+        same = [bool(torch.equal(a, b.detach())) for a, b in zip(flat, single)]
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok", same))
+    except Exception as e:
+        q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+def test_two_gpu_sharded_muon_matches_single_process(cuda_device):
+    """ShardedMuon on two GPUs (gradient reduce-scatter, local momentum, grouped
+    orthogonalization, in-place all-gather over NCCL): after two steps every
+    rank holds, bit for bit, the banks one process computes with Muon from
+    the averaged gradients."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_muon_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, status, res = q.get(timeout=240)
+            results[rank] = (status, res)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank in range(2):
+        status, res = results[rank]
+        assert status == "ok", res
+        assert all(res), res
