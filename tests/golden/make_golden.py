@@ -59,10 +59,14 @@ def certified(reference):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference project")
-    ap.add_argument("--only", choices=["all", "certified"], default="all",
-                    help="'certified' writes certified_circuits.json alone")
+    ap.add_argument("--only", choices=["all", "certified", "circuits"], default="all",
+                    help="'certified' writes certified_circuits.json alone; 'circuits' the whole-circuit "
+                         "fixtures alone")
+    ap.add_argument("--missing", action="store_true",
+                    help="write only fixtures that do not exist yet (existing files stay byte for byte)")
     args = ap.parse_args()
-    certified(os.path.abspath(args.reference))
+    if args.only in ("all", "certified"):
+        certified(os.path.abspath(args.reference))
     if args.only == "certified":
         return
     os.environ["TRITON_INTERPRET"] = "1"
@@ -85,6 +89,37 @@ def main():
         np.savez_compressed(path, **{k: v.numpy() if hasattr(v, "numpy") else np.asarray(v)
                                      for k, v in arrays.items()})
         print("wrote", path)
+
+    def exists(name):
+        return args.missing and os.path.exists(os.path.join(HERE, name))
+
+    # ---- whole circuits through the reference evaluator and Triton backend
+    cases = [
+        ("PS2_55", (1, 128, 256), 10),
+        ("PS3_55", (1, 128, 256), 11),
+        ("POLAR_EXPRESS", (1, 128, 256), 12),
+        ("JORDAN", (1, 128, 256), 13),
+        ("PS2_55", (2, 192, 64), 14),
+        ("PS3_55", (1, 96, 96), 15),
+        ("PS2_512", (1, 64, 160), 16),
+        ("PS2_64", (1, 128, 256), 30),
+        ("PS2_54", (1, 128, 256), 31),
+        ("PS2_4111", (1, 128, 256), 32),
+        ("PS2_11111", (1, 128, 256), 33),
+        ("PS3_64", (1, 128, 256), 34),
+        ("PS3_54", (1, 128, 256), 35),
+    ]
+    for method, shape, seed in cases:
+        name = f"circuit_{method}_{'x'.join(map(str, shape))}"
+        if exists(name + ".npz"):
+            continue
+        table = getattr(coefficients, method)
+        nbuf = 1 + max(max(w, i, r) for _, steps in table for w, i, r, *_ in steps)
+        Xc = randn(shape, seed)
+        Y = ref._run(Xc, table, triton_kernels, 1e-7, nbuf)
+        save(name, x=Xc, out=Y)
+    if args.only == "circuits":
+        return
 
     # ---- the coefficient data (tables and GNS preset) of the reference
     import json
@@ -126,23 +161,6 @@ def main():
             Y = triton_kernels.apply(Xa, B, tall, residual)
             save(f"op_apply_{'tall' if tall else 'wide'}_{'res' if residual else 'nores'}",
                  x=Xa, b=B, out=Y, residual=residual)
-
-    # ---- whole circuits through the reference evaluator and Triton backend
-    cases = [
-        ("PS2_55", (1, 128, 256), 10),
-        ("PS3_55", (1, 128, 256), 11),
-        ("POLAR_EXPRESS", (1, 128, 256), 12),
-        ("JORDAN", (1, 128, 256), 13),
-        ("PS2_55", (2, 192, 64), 14),
-        ("PS3_55", (1, 96, 96), 15),
-        ("PS2_512", (1, 64, 160), 16),
-    ]
-    for method, shape, seed in cases:
-        table = getattr(coefficients, method)
-        nbuf = 1 + max(max(w, i, r) for _, steps in table for w, i, r, *_ in steps)
-        Xc = randn(shape, seed)
-        Y = ref._run(Xc, table, triton_kernels, 1e-7, nbuf)
-        save(f"circuit_{method}_{'x'.join(map(str, shape))}", x=Xc, out=Y)
 
     # ---- the reference CPU path: requested PS2_55, runs POLAR_EXPRESS in torch
     import warnings

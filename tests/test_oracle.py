@@ -59,7 +59,9 @@ def test_apply(name):
 
 
 CIRCUITS = [("PS2_55", "1x128x256"), ("PS3_55", "1x128x256"), ("POLAR_EXPRESS", "1x128x256"),
-            ("JORDAN", "1x128x256"), ("PS2_55", "2x192x64"), ("PS3_55", "1x96x96"), ("PS2_512", "1x64x160")]
+            ("JORDAN", "1x128x256"), ("PS2_55", "2x192x64"), ("PS3_55", "1x96x96"), ("PS2_512", "1x64x160"),
+            ("PS2_64", "1x128x256"), ("PS2_54", "1x128x256"), ("PS2_4111", "1x128x256"),
+            ("PS2_11111", "1x128x256"), ("PS3_64", "1x128x256"), ("PS3_54", "1x128x256")]
 
 
 @pytest.mark.parametrize("method,shape", CIRCUITS)
