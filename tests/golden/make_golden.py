@@ -59,9 +59,9 @@ def certified(reference):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference project")
-    ap.add_argument("--only", choices=["all", "certified", "circuits"], default="all",
+    ap.add_argument("--only", choices=["all", "certified", "circuits", "gns"], default="all",
                     help="'certified' writes certified_circuits.json alone; 'circuits' the whole-circuit "
-                         "fixtures alone")
+                         "fixtures alone; 'gns' the GNS fixtures alone")
     ap.add_argument("--missing", action="store_true",
                     help="write only fixtures that do not exist yet (existing files stay byte for byte)")
     args = ap.parse_args()
@@ -120,6 +120,9 @@ def main():
         save(name, x=Xc, out=Y)
     if args.only == "circuits":
         return
+    if args.only == "gns":
+        gns_fixtures(args, randn, save, exists, gns)
+        return
 
     # ---- the coefficient data (tables and GNS preset) of the reference
     import json
@@ -172,13 +175,21 @@ def main():
     assert polar.last_execution["effective"] == "POLAR_EXPRESS"
     save("cpu_path_ps2_55_128x256", x=Xcpu, out=Ycpu)
 
-    # ---- GNS recurrence with the reference's PyTorch backend (rectangular)
-    Xg = randn((2, 96, 224), 21)
+    gns_fixtures(args, randn, save, exists, gns)
+
+
+def gns_fixtures(args, randn, save, exists, gns):
+    """GNS recurrence with the reference's PyTorch backend (rectangular):
+    wide (X Xᵀ) and tall (XᵀX) inputs."""
     inst = gns.GramNewtonSchulz(ns_epsilon=1e-7, ns_use_kernels=False,
                                 ns_coefficients=gns.GNS_COEFFICIENTS,
                                 gram_newton_schulz_reset_iterations=[2], compile_kwargs=None)
-    Yg = inst._select_gram(Xg)
-    save("gns_torch_2x96x224", x=Xg, out=Yg)
+    for shape, seed in (((2, 96, 224), 21), ((2, 224, 96), 22), ((1, 64, 320), 23)):
+        name = f"gns_torch_{'x'.join(map(str, shape))}"
+        if exists(name + ".npz"):
+            continue
+        Xg = randn(shape, seed)
+        save(name, x=Xg, out=inst._select_gram(Xg))
 
 
 if __name__ == "__main__":

@@ -95,9 +95,11 @@ def test_reference_cpu_path_port_is_exact():
     assert torch.equal(got, g["out"])
 
 
-def test_gns_against_reference_torch_recurrence():
+@pytest.mark.parametrize("shape", ["2x96x224", "2x224x96", "1x64x320"])
+def test_gns_against_reference_torch_recurrence(shape):
+    """Wide (X Xᵀ) and tall (XᵀX) inputs through the reference's PyTorch GNS."""
     from polar_switch.gram_newton_schulz import GNS_COEFFICIENTS
-    g = load("gns_torch_2x96x224")
+    g = load(f"gns_torch_{shape}")
     got = og.gns_run(g["x"], GNS_COEFFICIENTS, acc=torch.float32, mirror=False)
     err = oc.relative_frobenius(got, g["out"].float())
     assert err < 3e-3, err
