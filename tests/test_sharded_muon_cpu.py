@@ -85,7 +85,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shapes, padding, steps, scale, q):
+def _worker(rank, world, port, shapes, padding, steps, scale, q, fail_rank=-1):
     try:
         import torch.distributed as dist
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -96,6 +96,8 @@ def _worker(rank, world, port, shapes, padding, steps, scale, q):
         opt = _CpuShardedMuon(banks, _orthogonalize, lr=LR, momentum=MOMENTUM, weight_decay=DECAY,
                               scale=scale, norm_log=log)
         assert (opt.world_size, opt.rank) == (world, rank)
+        if rank == fail_rank:
+            raise RuntimeError("injected failure on the host before the step")
         for step in range(steps):
             for b, gr in zip(banks, _grads(shapes, padding, rank, step)):
                 b.grad = gr
@@ -163,6 +165,31 @@ def test_sharded_muon_gloo_matches_single_process(world, shapes, padding, scale)
         for got, exp, (count, _, _) in zip(moms, exp_moms, shapes):
             n = count // world
             assert torch.equal(got, exp[r * n:(r + 1) * n])  # momentum of the local chunk only
+
+
+def test_rank_failure_before_the_step_is_reported():
+    """A rank that raises before the step: the other ends with an error from
+    its gradient scatter (peer gone, or the process-group timeout) instead of
+    hanging."""
+    shapes, padding = [(2, 32, 32)], [0]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, shapes, padding, 1, "rms", q, 1)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, res = q.get(timeout=180)
+            results[rank] = res
+    finally:
+        for p in procs:
+            p.join(timeout=10)
+            if p.is_alive():
+                p.kill()
+    assert isinstance(results[1], str) and "injected failure" in results[1]
+    assert isinstance(results[0], str)  # the surviving rank's collective failed
 
 
 def test_sharded_muon_world1_without_process_group():
