@@ -63,48 +63,123 @@ def make_banks(shapes, device, seed=0, scale=1.0):
             for L, r, c in shapes]
 
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per matrix of the
-# dominant kernel, from one ncu capture of each square kernel at the Qwen shape
-# (profiles/ps_gemm_square_qwen_n1024.md, one-CTA: 307.4 MB;
-# profiles/ps_gemm_pair_square_qwen_n1024.md, CTA pairs, the default for n = 1024:
-# 309.0 MB; each a launch over 64 matrices of n = 1024); scaled to a launch by
-# its number of matrices.
-TRAFFIC_BYTES_PER_MATRIX = {("square", 1024): 309.0e6 / 64}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per matrix of a
+# kernel class at one matrix size, from ncu captures of the current kernels:
+# profiles/dram_traffic.json maps "<class>_n<n>" to {"bytes_per_matrix": B,
+# "capture": "<what was captured>"}; a launch's traffic is B times the number
+# of matrices it processes. Absent file or key: traffic is reported as null.
+def load_traffic_table():
+    try:
+        with open(os.path.join(ROOT, "profiles", "dram_traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def roofline_entry(name, v, steps, n_dom, clocks, peaks, traffic_table):
+    """Roofline of one kernel class from its profiled launches.
+
+    achieved = algorithmic FLOPs (or bytes) per launch / mean launch time. The
+    bound is taken from arithmetic intensity: FLOPs per DRAM byte (measured
+    traffic when the table has it, else the algorithmic bytes) against the
+    ridge point peak_flops / peak_bandwidth. The tensor peak is the measured
+    burst figure when the run's SM clock median sat at its maximum (a kernel
+    timed in bursts), else the sustained figure; the HBM peak is the measured
+    copy bandwidth. Fallbacks (no MEASURED_PEAKS.json): 1590 / 1400 TFLOP/s and
+    6650 GB/s.
+    """
+    burst = peaks.get("bf16_tflops")
+    sustained = peaks.get("bf16_tflops_sustained")
+    hbm = peaks.get("hbm_gbs")
+    src = "measured (MEASURED_PEAKS.json)"
+    if burst is None or sustained is None or hbm is None:
+        burst, sustained, hbm, src = 1590.0, 1400.0, 6650.0, "fallback"
+    at_max = (clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
+              and clocks["sm_mhz"] >= 0.97 * clocks["sm_max_mhz"])
+    tpeak, tname = (burst, "burst") if at_max else (sustained, "sustained")
+    launches = max(v["launches"], 1)
+    sec = v["ms"] * 1e-3 / launches
+    flops = v["flops"] / launches
+    alg_bytes = v["bytes"] / launches
+    traffic, traffic_src = None, None
+    key = f"{name}_n{n_dom}"
+    if key in traffic_table and flops:
+        mats = flops / traffic_table[key].get("flops_per_matrix", float(n_dom) ** 3)
+        traffic = traffic_table[key]["bytes_per_matrix"] * mats
+        traffic_src = f"ncu dram read+write of {traffic_table[key]['capture']}, scaled to {mats:.0f} matrices"
+    ai = flops / (traffic or alg_bytes) if (traffic or alg_bytes) else float("inf")
+    ridge = tpeak * 1e12 / (hbm * 1e9)
+    tensor = {"achieved": flops / sec / 1e12, "peak": tpeak, "frac": flops / sec / 1e12 / tpeak}
+    mem = {"achieved": (traffic or alg_bytes) / sec / 1e9, "peak": hbm,
+           "frac": (traffic or alg_bytes) / sec / 1e9 / hbm}
+    bound = "hbm" if ai < ridge else "tensor"
+    main = mem if bound == "hbm" else tensor
+    return {"bound": bound, "kernel": f"ps_gemm ({name})", "achieved": main["achieved"],
+            "peak": main["peak"], "unit": "GB/s" if bound == "hbm" else "TFLOP/s", "frac": main["frac"],
+            "peak_source": f"{src}: {'HBM copy' if bound == 'hbm' else 'bf16 ' + tname}",
+            "traffic": traffic, "traffic_source": traffic_src,
+            "arithmetic_intensity": ai, "ridge": ridge,
+            "tensor_frac": tensor["frac"], "tensor_tflops": tensor["achieved"],
+            "hbm_frac": mem["frac"], "hbm_gbs": mem["achieved"],
+            "launches_per_step": v["launches"] / steps, "ms_per_launch": sec * 1e3}
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples during the timed region: one
+    `nvidia-smi -lms` process samples every `period_ms` until the block exits;
+    entering waits (up to 5 s) for its first sample so the samples cover the
+    region that follows."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, period_ms=50):
         self.gpu_index = gpu_index
+        self.period_ms = period_ms
         self.samples = []
-        self._stop = threading.Event()
+        self._proc = None
         self._thread = None
+        self._first = threading.Event()
 
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([v.strip() for v in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+    def _read(self):
+        for line in self._proc.stdout:
+            vals = [v.strip() for v in line.strip().split(",")]
+            if len(vals) >= 9:
+                self.samples.append(vals)
+                self._first.set()
 
     def __enter__(self):
-        self._thread = threading.Thread(target=self._run, daemon=True)
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", f"-lms={self.period_ms}"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._proc = None
+            return self
+        self._thread = threading.Thread(target=self._read, daemon=True)
         self._thread.start()
+        self._first.wait(5.0)
+        self.samples.clear()  # keep only samples taken from here on
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        self._thread.join(timeout=10)
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._thread.join(timeout=5)
 
     def summary(self):
         if not self.samples:
@@ -196,10 +271,15 @@ def run_reference(args, world, rank):
             times.append(s)
     step_s = statistics.median(times)
     value = flops / step_s / 1e12
+    # Each "step" of this arm runs one layer of the workload (a bounded
+    # sample); ms_per_step is that sample's time, and the full step's time is
+    # the extrapolation over all layers, from which `value` is computed.
+    layers = min(L for L, _, _ in shapes)
     line = {
         "impl": "reference", "metric": "muon_step_orthogonalize_tflops" if args.workload != "single"
         else "orthogonalize_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3 / layers,
+        "ms_per_full_step_extrapolated": step_s * 1e3, "sample_per_step": f"1 of {layers} layers",
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic", "config": config_dict(args, shapes, method),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
@@ -292,6 +372,37 @@ PUBLISHED_MS = {
 }
 
 
+def time_single_8192(device, warmup, calls=15):
+    """The 8192 x 8192 PS2-55 circuit of the reference's published B200 heatmap
+    (7.47 ms median, README.md:77-81), timed call by call with CUDA events on
+    FP16 N(0, 1) input; median over `calls` after a warm-up."""
+    from polar_switch import circuit_flops, coefficients, make_polynomial_orthogonalizer
+    g = torch.Generator(device=device).manual_seed(0)
+    X = torch.randn(8192, 8192, generator=g, device=device, dtype=torch.float16)
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    Y = torch.empty_like(X)
+    flops = circuit_flops(coefficients.PS2_55, 8192, 8192)
+    for _ in range(max(warmup, 3)):
+        polar(X, out=Y)
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    with ClockSampler(device.index or 0) as clocks:
+        for _ in range(calls):
+            s.record()
+            polar(X, out=Y)
+            e.record()
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+    times.sort()
+    ms = times[len(times) // 2]
+    del X, Y
+    torch.cuda.empty_cache()
+    return {"shape": [8192, 8192], "method": "PS2_55", "input": "fp16 N(0,1), seed 0",
+            "calls": calls, "median_ms": ms, "min_ms": times[0], "tflops": flops / (ms * 1e-3) / 1e12,
+            "published_ms": 7.47, "vs_published": 7.47 / ms, "clocks": clocks.summary()}
+
+
 def run_sweep(args):
     """--sweep: median latency of whole circuits on the shapes whose reference
     latency is published, one JSON line per (shape, method). Inputs are FP16
@@ -356,6 +467,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-single", dest="single", action="store_false",
+                    help="skip the 8192 x 8192 PS2-55 point timed after the step at N = 1")
     ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize"],
                     help="time one kernel class alone (for profiling) instead of the whole step")
     ap.add_argument("--bank", type=int, default=0, help="bank of the workload used by --kernel")
@@ -486,25 +599,17 @@ def main():
         cpu_baseline = {"value": flops / step_s / 1e12, "unit": "TFLOP/s",
                         "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
 
+    single = None
+    if world == 1 and args.single and args.workload != "single":
+        single = time_single_8192(device, args.warmup)
+
     if rank == 0:
-        peaks = {}
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                peaks = json.load(f)
-        except OSError:
-            pass
+        peaks = load_peaks()
+        clock_summary = clocks.summary()
         gemm_kinds = {k: v for k, v in prof.items() if k in ("gram", "square", "apply") and v["launches"]}
         dom_name, dom = max(gemm_kinds.items(), key=lambda kv: kv[1]["ms"])
-        achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
-        traffic = None
         n_dom = min(min(r, c) for _, r, c in shapes)
-        if (dom_name, n_dom) in TRAFFIC_BYTES_PER_MATRIX and dom["launches"]:
-            mats_per_launch = dom["flops"] / dom["launches"] / float(n_dom) ** 3
-            traffic = TRAFFIC_BYTES_PER_MATRIX[(dom_name, n_dom)] * mats_per_launch
-        peak = peaks.get("bf16_tflops_sustained")
-        peak_src = "measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
-        if peak is None:
-            peak, peak_src = 1400.0, "fallback sustained"
+        roofline = roofline_entry(dom_name, dom, args.steps, n_dom, clock_summary, peaks, load_traffic_table())
         breakdown = {k: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
                          "tflops": (v["flops"] / (v["ms"] * 1e-3) / 1e12) if v["ms"] and v["flops"] else None,
                          "gbs": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) if v["ms"] else None}
@@ -515,19 +620,17 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": config_dict(args, shapes, method),
-            "roofline": {"bound": "tensor", "kernel": f"ps_gemm ({dom_name})", "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": peak_src, "traffic": traffic,
-                         "traffic_source": "ncu dram read+write bytes per launch (profiles/)" if traffic else None,
-                         "launches_per_step": dom["launches"] / args.steps},
+            "roofline": roofline,
             "kernels": breakdown,
             "cpu_baseline": cpu_baseline,
-            "clocks": clocks.summary(),
+            "clocks": clock_summary,
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "host_enqueue_ms_per_step": host_ms,
         }
+        if single is not None:
+            line["single_8192"] = single
         line["config"]["cuda_graph"] = bool(args.graph)
         if world > 1:
             line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),

@@ -10,6 +10,12 @@
  * Return value: PS_OK (0) or a negative PS_ERR_* code; ps_last_error()
  * returns a message for the calling thread's last failure.
  *
+ * Device state: per device, the first call looks up the device addresses of
+ * the library's module variables (the status word, the ps_normalize_noalloc
+ * scratch) and caches them for the life of the process. The library does not
+ * survive a cudaDeviceReset() or a destroyed and recreated primary context on
+ * a device it has already used: those cached addresses go stale.
+ *
  * FP16 matrices passed to gram/square/sym_product/apply are row-major with a
  * row pitch (`*_ld`, in elements) that is a multiple of 8, on 16-byte aligned
  * addresses; batch `l` starts at `ptr + l * rows * ld`.
@@ -108,7 +114,7 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
  * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);
 
-/* Caps the number of CTAs/* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
+/* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
  * afterwards; 0 (default) = every SM. Leaving SMs free lets a collective on
  * another stream run beside the GEMMs. Returns the previous cap. */
 PS_API int ps_set_max_ctas(int max_ctas);
@@ -134,8 +140,11 @@ PS_API int ps_normalize(const void* x, int x_dtype, int64_t L, int64_t rows, int
  * library, PS_NORMALIZE_NOALLOC_MAX_PARTIALS doubles (256 KiB), which every
  * GPU that loads the library keeps until the process exits.
  *
- * Same arguments and result as ps_normalize without the workspace. L must be
- * at most PS_NORMALIZE_NOALLOC_MAX_PARTIALS (PS_ERR_UNSUPPORTED otherwise).
+ * Same arguments as ps_normalize without the workspace. While the L matrices'
+ * partial sums (ps_normalize's chunking) fit the scratch, the result is the
+ * same bits as ps_normalize; beyond that each matrix is summed over fewer,
+ * longer chunks, which can move an output by one FP16 rounding step. L must
+ * be at most PS_NORMALIZE_NOALLOC_MAX_PARTIALS (PS_ERR_UNSUPPORTED otherwise).
  * Calls no allocating routine. The first call on a device looks up the
  * scratch's device address (cudaGetSymbolAddress), so make that first call
  * before any stream capture. All calls on a device share the scratch: calls
@@ -221,7 +230,7 @@ PS_API int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer,
                               int buffers, float eps, void* workspace, int64_t workspace_bytes,
                               void* stream);
 
-/* Scratch bytes ps_gns needs/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
+/* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 
 /* Gram Newton-Schulz on rectangular matrices (replaces the rectangular branch

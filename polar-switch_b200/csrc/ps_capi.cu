@@ -301,8 +301,7 @@ int launch_gemm_pair(int variant, const CUtensorMap& ta, const CUtensorMap& ta2,
   attr.val.clusterDim.x = 2;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = 1;
-  cudaLaunchConfig_t cfg;
-  std::memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(ps::pair::NUM_THREADS);
   cfg.dynamicSmemBytes = ps::pair::SMEM_TOTAL;
   cfg.stream = stream;

@@ -63,6 +63,31 @@ def muon_directions(grads, moms, momentum, out_dtype, nesterov=True):
     return out
 
 
+def fused_direction_ok(params, grads, moms):
+    """Whether ps_muon_direction can take this bucket: every momentum buffer
+    contiguous and every gradient and buffer in the parameters' dtype (a
+    non-contiguous gradient is copied to a contiguous one first). Otherwise
+    the bucket takes the reference's elementwise sequence: a parameter that is
+    a transposed view has a momentum buffer with its strides (zeros_like keeps
+    them), and FP32 gradients on BF16 weights promote the direction to FP32."""
+    dtype = params[0].dtype
+    return (dtype in (torch.float32, torch.bfloat16, torch.float16)
+            and all(g.dtype == dtype for g in grads)
+            and all(m.dtype == dtype and m.is_contiguous() for m in moms))
+
+
+def reference_directions(grads, moms, momentum, rms):
+    """The reference's direction step for one bucket (training/muon.py:66-76),
+    in torch: buf <- momentum * buf + g; d = g + momentum * buf; the stacked
+    directions cast to BF16 for the "rms" scale, else kept in the promoted dtype."""
+    directions = []
+    for g, buf in zip(grads, moms):
+        buf.mul_(momentum).add_(g)
+        directions.append(g.add(buf, alpha=momentum))
+    update = torch.stack(directions)
+    return update.bfloat16() if rms else update
+
+
 def muon_update(params, update, decay, alpha):
     """p <- p * decay + alpha * u for each matrix p and its row u of the stacked
     `update`, rounded like torch's p.mul_(decay); p.add_(u.to(p.dtype), alpha)."""
@@ -111,9 +136,14 @@ class Muon(torch.optim.Optimizer):
                         state["momentum_buffer"] = torch.zeros_like(p)
                     moms.append(state["momentum_buffer"])
                 # BF16 directions for the "rms" scale, as the reference passes them.
-                out_dtype = torch.bfloat16 if group["scale"] == "rms" else params[0].dtype
-                stacked.append(muon_directions([p.grad.contiguous() for p in params], moms,
-                                               group["momentum"], out_dtype))
+                rms = group["scale"] == "rms"
+                grads = [p.grad for p in params]
+                if fused_direction_ok(params, grads, moms):
+                    out_dtype = torch.bfloat16 if rms else params[0].dtype
+                    stacked.append(muon_directions([g.contiguous() for g in grads], moms,
+                                                   group["momentum"], out_dtype))
+                else:
+                    stacked.append(reference_directions(grads, moms, group["momentum"], rms))
                 members.append(params)
             grouped = getattr(self.orthogonalize, "grouped", None)
             updates = grouped(stacked) if grouped is not None else [self.orthogonalize(u) for u in stacked]

@@ -118,3 +118,47 @@ def test_sharded_muon_world1_equals_muon(cuda_device):
     for a, b in zip(flat, single):
         assert torch.equal(a, b.detach())
     assert not sharded[1][3:].any()
+
+
+def test_transposed_view_parameters_take_the_reference_sequence(cuda_device):
+    """A parameter that is a transposed view has a momentum buffer with its
+    strides (zeros_like keeps them); the reference accepts it, and so must the
+    drop-in: same bits as the reference rule on the same orthogonalizer."""
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    base = [seeded((384, 256), 700 + i).to(cuda_device) * 0.02 for i in range(3)]
+    params = [torch.nn.Parameter(b.clone().mT) for b in base]  # (256, 384), not contiguous
+    assert not params[0].is_contiguous()
+    ref_params = [b.clone().mT for b in base]
+    ref_moms = [torch.zeros_like(p) for p in ref_params]
+    opt = Muon([{"params": params, "role": "attn"}], polar, lr=0.02, weight_decay=0.1)
+    for step in range(2):
+        grads = [seeded((256, 384), 710 + 10 * step + i).to(cuda_device) for i in range(3)]
+        for p, g in zip(params, grads):
+            p.grad = g.clone()
+        opt.step()
+        _reference_step(ref_params, grads, ref_moms, polar, 0.02, 0.95, 0.1)
+    for p, r, m in zip(params, ref_params, ref_moms):
+        assert torch.equal(p.detach(), r)
+        assert torch.equal(opt.state[p]["momentum_buffer"], m)
+
+
+def test_fp32_gradients_on_bf16_weights(cuda_device):
+    """FP32 gradients on BF16 weights: the reference adds them into the BF16
+    momentum buffer and forms FP32 directions; the drop-in keeps going the same
+    way (momentum bit for bit, parameters within the fused update's rounding)."""
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    shapes = [(256, 512)] * 2
+    params = [torch.nn.Parameter((seeded(s, 720 + i) * 0.02).to(cuda_device, torch.bfloat16))
+              for i, s in enumerate(shapes)]
+    ref_params = [p.detach().clone() for p in params]
+    ref_moms = [torch.zeros_like(p) for p in ref_params]
+    opt = Muon([{"params": params, "role": "mlp"}], polar, lr=0.02, weight_decay=0.1)
+    for step in range(2):
+        grads = [seeded(s, 730 + 10 * step + i).to(cuda_device) for i, s in enumerate(shapes)]
+        for p, g in zip(params, grads):
+            p.grad = g.clone()  # FP32 gradient on a BF16 parameter
+        opt.step()
+        _reference_step(ref_params, grads, ref_moms, polar, 0.02, 0.95, 0.1)
+    for p, r, m in zip(params, ref_params, ref_moms):
+        assert torch.equal(opt.state[p]["momentum_buffer"], m)
+        assert float((p.detach().float() - r.float()).norm() / r.float().norm()) < 1e-3

@@ -78,3 +78,20 @@ def test_host_side_knobs_round_trip_without_gpu():
     assert lib.ps_set_max_ctas(-5) == _native.PS_ERR_INVALID
     assert lib.ps_set_max_ctas(100) == 0
     assert lib.ps_set_max_ctas(0) == 100
+
+
+def test_public_header_compiles_cleanly_as_c_and_cpp(tmp_path):
+    """The ABI header is included by C and C++ consumers: it must compile with
+    -Wall -Wextra -Werror in both languages (a stray comment opener inside a
+    comment, for one, trips -Wcomment)."""
+    import shutil
+    import subprocess
+    src = tmp_path / "use_header.c"
+    src.write_text('#include "polar_switch_b200.h"\nint main(void) { return PS_OK; }\n')
+    inc = os.path.join(ROOT, "include")
+    for cc, extra in (("gcc", []), ("g++", ["-x", "c++"])):
+        if shutil.which(cc) is None:
+            continue
+        r = subprocess.run([cc, "-Wall", "-Wextra", "-Werror", *extra, "-I", inc, "-c", str(src),
+                            "-o", str(tmp_path / f"o_{cc}.o")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
