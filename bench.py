@@ -307,7 +307,18 @@ def run_kernel(args):
     device = torch.device("cuda", 0)
     shapes = bank_shapes(args.workload)
     g = torch.Generator(device=device).manual_seed(0)
-    if args.kernel in ("square", "sym_product"):
+    if args.kernel == "chain":
+        # all inner iterations of the workload's squares as the circuit runs
+        # them: whole PS2-55 circuits on L square matrices of the bank's n
+        from polar_switch import make_polynomial_orthogonalizer
+        n = min(shapes[args.bank][1:])
+        L = args.L or sum(Lg for Lg, r, c in shapes if min(r, c) == n)
+        X = torch.randn(L, n, n, generator=g, device=device)
+        Y = torch.empty_like(X)
+        polar = make_polynomial_orthogonalizer("PS2_55")
+        fn = lambda: polar(X, out=Y)  # noqa: E731
+        desc = f"chain (PS2_55 circuits) L={L} n={n}"
+    elif args.kernel in ("square", "sym_product"):
         n = min(shapes[args.bank][1:])
         L = args.L or sum(Lg for Lg, r, c in shapes if min(r, c) == n)
         X = torch.randn(L, n, 2 * n, generator=g, device=device)
@@ -345,7 +356,7 @@ def run_kernel(args):
         fn()
     prof = nat.profile_read()
     nat.profile_enable(False)
-    kind = {"square": "square", "sym_product": "square"}.get(args.kernel, args.kernel)
+    kind = {"square": "square", "sym_product": "square", "chain": "square"}.get(args.kernel, args.kernel)
     v = prof[kind]
     ms = v["ms"] / max(v["launches"], 1)
     print(json.dumps({"kernel": desc, "ms_per_launch": ms, "launches": v["launches"],
@@ -469,7 +480,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-single", dest="single", action="store_false",
                     help="skip the 8192 x 8192 PS2-55 point timed after the step at N = 1")
-    ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize"],
+    ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize", "chain"],
                     help="time one kernel class alone (for profiling) instead of the whole step")
     ap.add_argument("--bank", type=int, default=0, help="bank of the workload used by --kernel")
     ap.add_argument("--L", type=int, default=0, help="--kernel: override the number of matrices")

@@ -94,6 +94,17 @@ PS_API int ps_set_wait_limit(long long cycles);
  * tests of the bounded-wait path. */
 PS_API int ps_selftest_wait(long long limit_cycles, void* stream);
 
+/* Launches one chain kernel (see ps_set_chain) whose second inner iteration
+ * waits for a completion count that never arrives: those waits run out after
+ * `limit_cycles` and record status code 6 (dependency timeout), and the
+ * kernel returns early. `workspace`: at least PS_SELFTEST_CHAIN_WORKSPACE_BYTES
+ * of device memory, 16-byte aligned (overwritten). limit_cycles must be at
+ * most a quarter of the ps_set_wait_limit value. Used by the tests of the
+ * bounded-wait path of the chain kernel. */
+#define PS_SELFTEST_CHAIN_WORKSPACE_BYTES (1 << 20)
+PS_API int ps_selftest_chain_wait(void* workspace, int64_t workspace_bytes, long long limit_cycles,
+                                  void* stream);
+
 /* Number of kernels this library has launched in the process so far. */
 PS_API long long ps_launch_count(void);
 
@@ -113,6 +124,16 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
  * one-CTA kernel for everything else. All compute the same products with the
  * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);
+
+/* How the inner iterations of ps_circuit / ps_circuit_grouped run on the
+ * CTA-pair path (square buffers with n <= 1024): 1 (default) = one persistent
+ * launch per outer iteration for all of them ("chain": a step of a matrix
+ * starts as soon as that matrix's previous step is stored, so its buffers are
+ * reused from L2), 0 = one launch per inner iteration. Same bits either way.
+ * Returns the previous mode (PS_ERR_INVALID for other values). No counterpart
+ * in the reference (its inner loop, polar_switch/__init__.py:42-43, issues one
+ * kernel per inner iteration). */
+PS_API int ps_set_chain(int mode);
 
 /* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
  * afterwards; 0 (default) = every SM. Leaving SMs free lets a collective on

@@ -20,6 +20,7 @@
 #include "../../include/polar_switch_b200.h"
 #include "ps_gemm.cuh"
 #include "ps_gemm2.cuh"
+#include "ps_chain.cuh"
 #include "ps_norm.cuh"
 #include "ps_muon.cuh"
 #include "ps_stats.cuh"
@@ -65,6 +66,10 @@ constexpr int64_t kPairMaxN = 1024;
 // Upper bound on the CTAs (SMs) a persistent GEMM grid may take; 0 = all SMs.
 // Leaving SMs free lets a collective run beside the GEMMs.
 int g_max_ctas = 0;
+// Inner iterations of a grouped circuit on the CTA-pair path run as one
+// persistent chain launch per outer iteration (1, default) or one launch per
+// inner iteration (0). Both give the same bits.
+int g_chain_mode = 1;
 
 // Every kernel launch of the library is counted; when profiling is enabled,
 // each launch is also bracketed by CUDA events on its stream and tagged with
@@ -139,6 +144,8 @@ struct DeviceState {
   bool smem_attr[kNumVariants] = {};
   bool pair_ready[kNumVariants] = {};
   int pair_clusters[kNumVariants] = {};
+  bool chain_ready = false;
+  int chain_clusters = 0;
 };
 
 std::mutex g_mu;
@@ -470,6 +477,119 @@ int launch_gemm(int variant, const CUtensorMap& ta, const CUtensorMap& tb, const
     return PS_OK;
   }
   return launch_jobs<A_MN, B_MN, SYM, OUT>(&job, 1, stream);
+}
+
+// ------------------------------------------------------------------ chain
+// Whether the inner iterations of an n-group run as chain launches.
+bool use_chain(int64_t n, int buffers) {
+  return g_chain_mode && use_pair(true, n) && buffers <= ps::chain::MAX_BUFS;
+}
+
+// Pair tiles of one n x n symmetric product (column pair p owns row pairs 0..p).
+int pair_sym_tiles(int64_t n) {
+  const int tb = static_cast<int>((n + ps::pair::BM - 1) / ps::pair::BM);
+  const int P = (tb + 1) / 2;
+  return P * (P + 1) / 2;
+}
+
+// Inner iterations steps[0..S) (S <= MAX_STEPS) of L triangle-stored n x n
+// buffers (buffer k at bufs + k * buf_bytes) as one chain launch. `done`
+// holds L counters whose value at the launch is `base`; every pair tile adds
+// SIGNALS_PER_TILE to its matrix's counter.
+int chain_launch(uint8_t* bufs, int64_t buf_bytes, int buffers, int64_t L, int64_t n,
+                 const ps_step* steps, int S, unsigned* done, unsigned base, cudaStream_t stream,
+                 long long dep_limit = 0) {
+  using ps::chain::ChainParams;
+  if (S < 1 || S > ps::chain::MAX_STEPS || buffers > ps::chain::MAX_BUFS)
+    return fail(PS_ERR_INVALID, "internal: chain of %d steps over %d buffers", S, buffers);
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  auto kern = ps::chain::ps_chain_pair_kernel;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(ps::pair::NUM_THREADS);
+  cfg.dynamicSmemBytes = ps::pair::SMEM_TOTAL;
+  cfg.stream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  if (!st->chain_ready) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         ps::pair::SMEM_TOTAL);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain smem)");
+    cfg.gridDim = dim3(2 * (st->sms / 2));
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters(chain)");
+    if (clusters < 1) return fail(PS_ERR_UNSUPPORTED, "no co-resident CTA pair fits on the device");
+    st->chain_clusters = clusters;
+    st->chain_ready = true;
+  }
+  // Params are large (~6 KB); kept off the stack.
+  static thread_local ChainParams P;
+  std::memset(&P, 0, sizeof(P));
+  for (int k = 0; k < buffers; ++k) {
+    void* ptr = bufs + k * buf_bytes;
+    if ((rc = map_kmajor(&P.tmK[k], ptr, n, n, L, n, n * n, ps::pair::BM))) return rc;
+    if ((rc = map_mnmajor(&P.tmMN[k], ptr, n, n, L, n, n * n))) return rc;
+    if ((rc = map_out(&P.tmD[k], ptr, PS_F16, n, n, L, n, n * n))) return rc;
+    P.buf[k] = static_cast<const __half*>(ptr);
+  }
+  for (int i = 0; i < S; ++i)
+    P.steps[i] = {steps[i].dst, steps[i].src, steps[i].add, steps[i].alpha, steps[i].beta,
+                  steps[i].diag};
+  const int T = pair_sym_tiles(n);
+  int pairs = st->chain_clusters;
+  if (g_max_ctas > 1 && pairs > g_max_ctas / 2) pairs = g_max_ctas / 2;
+  // Chunk size: the tile a producer waits for (step s - 1 of its matrix) was
+  // scheduled S chunks earlier; make that about two waves of pair tiles, and
+  // keep the item table within MAX_ITEMS.
+  int64_t C = (2LL * pairs + static_cast<int64_t>(S) * T - 1) / (static_cast<int64_t>(S) * T);
+  if (C < 1) C = 1;
+  const int64_t c_min = (L * S + ps::chain::MAX_ITEMS - 1) / ps::chain::MAX_ITEMS;
+  if (C < c_min) C = c_min;
+  if (C > L) C = L;
+  const int64_t nch = (L + C - 1) / C;
+  int items = 0;
+  int64_t tiles = 0;
+  for (int64_t round = 0; round < nch + S - 1; ++round) {
+    for (int s = 0; s < S; ++s) {
+      const int64_t c = round - s;
+      if (c < 0 || c >= nch) continue;
+      P.item_start[items] = static_cast<int>(tiles);
+      P.item_step[items] = static_cast<unsigned short>(s);
+      P.item_chunk[items] = static_cast<unsigned short>(c);
+      ++items;
+      const int64_t size = std::min<int64_t>(C, L - c * C);
+      tiles += size * T;
+    }
+  }
+  if (tiles > INT32_MAX) return fail(PS_ERR_UNSUPPORTED, "chain: too many tiles");
+  P.item_start[items] = static_cast<int>(tiles);
+  P.n_items = items;
+  P.total_tiles = static_cast<int>(tiles);
+  P.n = static_cast<int>(n);
+  P.L = static_cast<int>(L);
+  P.T = T;
+  P.chunk = static_cast<int>(C);
+  P.nbufs = buffers;
+  P.base = base;
+  P.done = done;
+  P.status = st->status;
+  P.wait_limit = g_wait_limit;
+  P.dep_limit = dep_limit > 0 ? dep_limit : g_wait_limit;
+  if (pairs > P.total_tiles) pairs = P.total_tiles;
+  cfg.gridDim = dim3(2 * pairs);
+  const double nn = static_cast<double>(n) * n;
+  LaunchScope scope(kProfSquare, stream, static_cast<double>(S) * L * nn * n,
+                    static_cast<double>(S) * L * nn * 2.0 * 3.0);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
+  if (e != cudaSuccess) return cuda_fail(e, "chain launch");
+  return PS_OK;
 }
 
 void fill_sym_tiles(ps::GemmArgs& a, int64_t n, int64_t L) {
@@ -1005,9 +1125,11 @@ struct GroupedPlan {
   };
   struct NGroup {
     int64_t n, Ltot, buf_off, buf_bytes;
+    int64_t ctr_off;  // per-matrix completion counters of chain launches
   };
   std::vector<Prob> probs;
   std::vector<NGroup> groups;
+  int64_t ctr_off = 0, ctr_bytes = 0;  // all groups' counters, one contiguous range
   int64_t total = 0;
 };
 
@@ -1027,7 +1149,7 @@ int make_grouped_plan(const ps_problem* probs, int n_probs, int buffers, int sms
     for (size_t k = 0; k < plan->groups.size(); ++k)
       if (plan->groups[k].n == p.lay.n) g = static_cast<int>(k);
     if (g < 0) {
-      plan->groups.push_back({p.lay.n, 0, 0, 0});
+      plan->groups.push_back({p.lay.n, 0, 0, 0, 0});
       g = static_cast<int>(plan->groups.size()) - 1;
     }
     p.group = g;
@@ -1046,6 +1168,12 @@ int make_grouped_plan(const ps_problem* probs, int n_probs, int buffers, int sms
     p.norm_off = off;
     off += p.lay.norm_bytes;
   }
+  plan->ctr_off = off;
+  for (GroupedPlan::NGroup& g : plan->groups) {
+    g.ctr_off = off;
+    off += round_up(g.Ltot * static_cast<int64_t>(sizeof(unsigned)), 256);
+  }
+  plan->ctr_bytes = off - plan->ctr_off;
   plan->total = off;
   return PS_OK;
 }
@@ -1233,6 +1361,13 @@ int ps_set_cta_pairs(int mode) {
   return previous;
 }
 
+int ps_set_chain(int mode) {
+  if (mode < 0 || mode > 1) return fail(PS_ERR_INVALID, "ps_set_chain: mode must be 0 or 1");
+  const int previous = g_chain_mode;
+  g_chain_mode = mode;
+  return previous;
+}
+
 int ps_set_wait_limit(long long cycles) {
   if (cycles <= 0) return fail(PS_ERR_INVALID, "ps_set_wait_limit: cycles must be positive");
   g_wait_limit = cycles;
@@ -1248,6 +1383,28 @@ int ps_selftest_wait(long long limit_cycles, void* stream) {
                                                                                limit_cycles);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PS_OK : cuda_fail(e, "selftest launch");
+}
+
+int ps_selftest_chain_wait(void* workspace, int64_t workspace_bytes, long long limit_cycles,
+                           void* stream) {
+  if (!workspace || !aligned16(workspace))
+    return fail(PS_ERR_INVALID, "ps_selftest_chain_wait: null or misaligned workspace");
+  if (workspace_bytes < PS_SELFTEST_CHAIN_WORKSPACE_BYTES)
+    return fail(PS_ERR_WORKSPACE, "ps_selftest_chain_wait: workspace too small");
+  if (limit_cycles <= 0 || limit_cycles > g_wait_limit / 4)
+    return fail(PS_ERR_INVALID, "ps_selftest_chain_wait: limit must be positive and at most a "
+                                "quarter of the wait limit");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Two 256 x 256 matrices, two buffers, two inner iterations; the counters
+  // start far below what step 1 waits for, so every step-1 tile's wait runs
+  // out (after limit_cycles, before any mbarrier wait could).
+  const int64_t n = 256, L = 2, buf_bytes = L * n * n * 2;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(ws, 0, 2 * buf_bytes + 256, s);
+  if (e != cudaSuccess) return cuda_fail(e, "ps_selftest_chain_wait memset");
+  const ps_step steps[2] = {{1, 0, 0, 1.f, 0.f, 0.f}, {0, 1, 1, 1.f, 0.f, 0.f}};
+  return chain_launch(ws, buf_bytes, 2, L, n, steps, 2,
+                      reinterpret_cast<unsigned*>(ws + 2 * buf_bytes), 0x40000000u, s, limit_cycles);
 }
 
 int64_t ps_normalize_workspace_bytes(int64_t L, int64_t rows, int64_t cols) {
@@ -1541,6 +1698,14 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
                 p.lay.Rp == q.rows && p.lay.Cp == q.cols &&
                 (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 && aligned16(q.y);
   }
+  // Chain launches count completed tiles per matrix from zero within this call.
+  std::vector<unsigned> chain_base(plan.groups.size(), 0u);
+  bool any_chain = false;
+  for (const GroupedPlan::NGroup& g : plan.groups) any_chain |= use_chain(g.n, buffers);
+  if (any_chain) {
+    cudaError_t e = cudaMemsetAsync(ws + plan.ctr_off, 0, plan.ctr_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "chain counters memset");
+  }
   int off = 0;
   for (int t = 0; t < n_outer; ++t) {
     // The Grams of all problems, batched into one launch per kernel variant.
@@ -1554,18 +1719,33 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
       }
       if ((rc = sink.flush(s))) return rc;
     }
-    int last = 0;
-    for (int k = 0; k < n_steps[t]; ++k) {
-      const ps_step& q = steps[off + k];
-      // One launch per distinct n covers the inner iteration of every problem.
-      for (const GroupedPlan::NGroup& g : plan.groups) {
-        uint8_t* base = ws + g.buf_off;
+    const int last = steps[off + n_steps[t] - 1].dst;
+    for (size_t gi = 0; gi < plan.groups.size(); ++gi) {
+      const GroupedPlan::NGroup& g = plan.groups[gi];
+      uint8_t* base = ws + g.buf_off;
+      if (use_chain(g.n, buffers)) {
+        // All inner iterations of this outer iteration in chain launches of
+        // up to MAX_STEPS steps each.
+        unsigned* done = reinterpret_cast<unsigned*>(ws + g.ctr_off);
+        const unsigned per_step =
+            static_cast<unsigned>(ps::chain::SIGNALS_PER_TILE * pair_sym_tiles(g.n));
+        for (int k0 = 0; k0 < n_steps[t]; k0 += ps::chain::MAX_STEPS) {
+          const int S = std::min(n_steps[t] - k0, ps::chain::MAX_STEPS);
+          if ((rc = chain_launch(base, g.buf_bytes, buffers, g.Ltot, g.n, steps + off + k0, S, done,
+                                 chain_base[gi], s)))
+            return rc;
+          chain_base[gi] += static_cast<unsigned>(S) * per_step;
+        }
+        continue;
+      }
+      // One launch per inner iteration covers every problem with this n.
+      for (int k = 0; k < n_steps[t]; ++k) {
+        const ps_step& q = steps[off + k];
         if ((rc = sym_product_impl(base + q.src * g.buf_bytes, base + q.src * g.buf_bytes,
                                    base + q.add * g.buf_bytes, base + q.dst * g.buf_bytes, g.Ltot,
                                    g.n, q.alpha, q.beta, q.diag, s, "ps_circuit(square)", tri)))
           return rc;
       }
-      last = q.dst;
     }
     off += n_steps[t];
     const bool final_iter = t == n_outer - 1;

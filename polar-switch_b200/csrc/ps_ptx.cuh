@@ -18,6 +18,7 @@ enum : int {
   kStatusEpilogueTimeout = 3,
   kStatusDrainTimeout = 4,
   kStatusSelftestTimeout = 5,
+  kStatusDependencyTimeout = 6,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -316,6 +317,49 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           bar_cluster)
       : "memory");
+}
+
+// ---------------------------------------------------------------- cross-CTA counters
+// A CTA publishes data it wrote with TMA stores by waiting for the stores
+// (bulk_wait<0>), fence_proxy_async_global(), then red_release_gpu_add on a
+// counter; a CTA that observes the count with ld_acquire_gpu_u32 issues
+// fence_proxy_async_global() before its TMA loads of that data.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add_u32(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until *ctr >= need, for at most `limit` SM clock cycles. Gives up
+// early when this CTA's abort flag is raised or another CTA has recorded an
+// error in the device status word; on timeout records `code` there.
+__device__ __forceinline__ bool counter_wait_bounded(const unsigned* ctr, unsigned need,
+                                                     volatile int* abort_flag, int* status,
+                                                     int code, long long limit) {
+  if (ld_acquire_gpu_u32(ctr) >= need) return true;
+  const long long start = clock64();
+  while (true) {
+    __nanosleep(32);
+    if (ld_acquire_gpu_u32(ctr) >= need) return true;
+    if (*abort_flag) return false;
+    if (status && *reinterpret_cast<volatile int*>(status) != 0) {
+      *abort_flag = 1;
+      return false;
+    }
+    if (clock64() - start > limit) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- misc

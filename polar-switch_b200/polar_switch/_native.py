@@ -25,10 +25,11 @@ DTYPE_CODES = {torch.float16: PS_F16, torch.float32: PS_F32, torch.bfloat16: PS_
 # Every symbol include/polar_switch_b200.h declares.
 EXPORTED = (
     "ps_version", "ps_last_error", "ps_get_status", "ps_set_wait_limit", "ps_selftest_wait",
+    "ps_selftest_chain_wait",
     "ps_normalize_workspace_bytes", "ps_normalize", "ps_gram", "ps_square", "ps_sym_product",
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
-    "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs",
+    "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs", "ps_set_chain",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
     "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
 )
@@ -69,6 +70,7 @@ _SIGNATURES = {
     "ps_get_status": ([ctypes.POINTER(_int), _int], _int),
     "ps_set_wait_limit": ([ctypes.c_longlong], _int),
     "ps_selftest_wait": ([ctypes.c_longlong, _ptr], _int),
+    "ps_selftest_chain_wait": ([_ptr, ctypes.c_int64, ctypes.c_longlong, _ptr], _int),
     "ps_normalize_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "ps_normalize": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _i64, _i64,
                       _ptr, _i64, _ptr], _int),
@@ -85,6 +87,7 @@ _SIGNATURES = {
                     _int, _f32, _ptr, _i64, _ptr], _int),
     "ps_launch_count": ([], ctypes.c_longlong),
     "ps_set_cta_pairs": ([_int], _int),
+    "ps_set_chain": ([_int], _int),
     "ps_set_max_ctas": ([_int], _int),
     "ps_gns_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "ps_sumsq": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr, _i64, _ptr], _int),
@@ -190,6 +193,15 @@ def set_cta_pairs(mode):
     rc = load().ps_set_cta_pairs(int(mode))
     if rc < 0:
         check("ps_set_cta_pairs", rc)
+    return rc
+
+
+def set_chain(mode):
+    """Inner iterations of grouped circuits on CTA pairs: 1 (default) one chain launch
+    per outer iteration, 0 one launch per inner iteration. Returns the previous mode."""
+    rc = load().ps_set_chain(int(mode))
+    if rc < 0:
+        check("ps_set_chain", rc)
     return rc
 
 

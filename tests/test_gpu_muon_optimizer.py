@@ -156,6 +156,7 @@ def test_fp32_gradients_on_bf16_weights(cuda_device):
     for step in range(2):
         grads = [seeded(s, 730 + 10 * step + i).to(cuda_device) for i, s in enumerate(shapes)]
         for p, g in zip(params, grads):
+            p.grad_dtype = None  # torch checks a gradient's dtype unless told not to
             p.grad = g.clone()  # FP32 gradient on a BF16 parameter
         opt.step()
         _reference_step(ref_params, grads, ref_moms, polar, 0.02, 0.95, 0.1)

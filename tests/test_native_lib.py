@@ -95,3 +95,16 @@ def test_public_header_compiles_cleanly_as_c_and_cpp(tmp_path):
         r = subprocess.run([cc, "-Wall", "-Wextra", "-Werror", *extra, "-I", inc, "-c", str(src),
                             "-o", str(tmp_path / f"o_{cc}.o")], capture_output=True, text=True)
         assert r.returncode == 0, r.stderr
+
+
+def test_chain_knob_and_selftest_arguments_without_gpu():
+    lib = _native.load()
+    assert lib.ps_set_chain(2) == _native.PS_ERR_INVALID
+    assert lib.ps_set_chain(-1) == _native.PS_ERR_INVALID
+    prev = lib.ps_set_chain(0)
+    assert prev == 1  # default: chain launches on
+    assert lib.ps_set_chain(prev) == 0
+    null = ctypes.c_void_p(0)
+    assert lib.ps_selftest_chain_wait(null, 1 << 20, 1000, null) == _native.PS_ERR_INVALID
+    assert lib.ps_selftest_chain_wait(ctypes.c_void_p(256), 1024, 1000, null) == _native.PS_ERR_WORKSPACE
+    assert lib.ps_selftest_chain_wait(ctypes.c_void_p(256), 1 << 20, 0, null) == _native.PS_ERR_INVALID
