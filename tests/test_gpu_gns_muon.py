@@ -219,15 +219,20 @@ def test_launch_counter_and_profiler(cuda_device):
     from polar_switch import make_polynomial_orthogonalizer
     polar = make_polynomial_orthogonalizer("PS2_55")
     X = seeded((2, 256, 512), 61).to(cuda_device)
-    n0 = nat.launch_count()
-    nat.profile_enable(True)
-    polar(X)
-    prof = nat.profile_read()
-    nat.profile_enable(False)
-    # 2 normalise + 2 x (1 gram + 5 squares + 1 apply)
-    assert nat.launch_count() - n0 == 16
-    assert prof["normalize"]["launches"] == 2
-    assert prof["gram"]["launches"] == 2 and prof["square"]["launches"] == 10
-    assert prof["apply"]["launches"] == 2
-    assert prof["square"]["flops"] == pytest.approx(10 * 2 * 256 ** 3)
-    assert all(v["ms"] > 0 for v in prof.values() if v["launches"])
+    for chain, squares in ((0, 10), (1, 2)):
+        prev = nat.set_chain(chain)
+        try:
+            n0 = nat.launch_count()
+            nat.profile_enable(True)
+            polar(X)
+            prof = nat.profile_read()
+            nat.profile_enable(False)
+        finally:
+            nat.set_chain(prev)
+        # 2 normalise + 2 x (1 gram + 5 squares (or one chain launch) + 1 apply)
+        assert nat.launch_count() - n0 == 6 + squares
+        assert prof["normalize"]["launches"] == 2
+        assert prof["gram"]["launches"] == 2 and prof["square"]["launches"] == squares
+        assert prof["apply"]["launches"] == 2
+        assert prof["square"]["flops"] == pytest.approx(10 * 2 * 256 ** 3)
+        assert all(v["ms"] > 0 for v in prof.values() if v["launches"])
