@@ -248,6 +248,34 @@ int map_mnmajor(CUtensorMap* m, const void* p, int64_t mn, int64_t k, int64_t L,
                 int64_t bs) {
   return make_map(m, p, PS_F16, mn, k, L, ld, bs, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
 }
+// Operand map for the CTA-pair kernel: with `inner` (the contiguous extent:
+// K for a K-major operand, M/N for an MN-major one) a multiple of 64, a 4-D
+// "chunked" view (64 | outer | inner / 64 | L) whose (64, 128, 2, 1) box is a
+// whole 128-wide K stage in one TMA (*chunked = 1); otherwise the 3-D map of
+// map_kmajor / map_mnmajor (*chunked = 0).
+int map_pair_operand(CUtensorMap* m, const void* p, bool mn_major, int64_t inner, int64_t outer,
+                     int64_t L, int64_t ld, int64_t bs, int* chunked) {
+  if (inner % 64 == 0) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(outer), static_cast<cuuint64_t>(inner / 64),
+                          static_cast<cuuint64_t>(L)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld * 2), 128, static_cast<cuuint64_t>(bs * 2)};
+    cuuint32_t box[4] = {64, 128, 2, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(p), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS) {
+      *chunked = 1;
+      return PS_OK;
+    }
+  }
+  *chunked = 0;
+  return mn_major ? map_mnmajor(m, p, inner, outer, L, ld, bs)
+                  : map_kmajor(m, p, inner, outer, L, ld, bs, ps::pair::BM);
+}
+
 // Output map: 32 x 32 sub-tiles, swizzle matching the epilogue's staging.
 int map_out(CUtensorMap* m, const void* p, int dtype, int64_t cols, int64_t rows, int64_t L,
             int64_t ld, int64_t bs) {
@@ -283,6 +311,10 @@ ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
   a.b_tri = g.b_tri;
   a.store_mirror = g.store_mirror;
   a.same_ab = g.same_ab;
+  a.a_chunk = g.a_chunk;
+  a.b_chunk = g.b_chunk;
+  a.a2_chunk = g.a2_chunk;
+  a.b2_chunk = g.b2_chunk;
   if (sym) {
     a.tb = (g.M + ps::pair::BM - 1) / ps::pair::BM;
     const int P = (a.tb + 1) / 2;
@@ -532,13 +564,19 @@ int chain_launch(uint8_t* bufs, int64_t buf_bytes, int buffers, int64_t L, int64
   // Params are large (~6 KB); kept off the stack.
   static thread_local ChainParams P;
   std::memset(&P, 0, sizeof(P));
+  int ck = 1, cm = 1;
   for (int k = 0; k < buffers; ++k) {
     void* ptr = bufs + k * buf_bytes;
-    if ((rc = map_kmajor(&P.tmK[k], ptr, n, n, L, n, n * n, ps::pair::BM))) return rc;
-    if ((rc = map_mnmajor(&P.tmMN[k], ptr, n, n, L, n, n * n))) return rc;
+    int c1 = 0, c2 = 0;
+    if ((rc = map_pair_operand(&P.tmK[k], ptr, false, n, n, L, n, n * n, &c1))) return rc;
+    if ((rc = map_pair_operand(&P.tmMN[k], ptr, true, n, n, L, n, n * n, &c2))) return rc;
     if ((rc = map_out(&P.tmD[k], ptr, PS_F16, n, n, L, n, n * n))) return rc;
     P.buf[k] = static_cast<const __half*>(ptr);
+    ck &= c1;
+    cm &= c2;
   }
+  if (ck != cm) return fail(PS_ERR_INVALID, "internal: chain operand maps disagree on the chunked layout");
+  P.chunked = ck;
   for (int i = 0; i < S; ++i)
     P.steps[i] = {steps[i].dst, steps[i].src, steps[i].add, steps[i].alpha, steps[i].beta,
                   steps[i].diag};
@@ -647,14 +685,19 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   // gemm_symmetric(A, B) even when B is symmetric only up to rounding.
   const bool same = p == q;
   const bool pair = use_pair(same, n);
-  if ((rc = map_kmajor(&ta, p, n, n, L, n, n * n, ps::BM))) return rc;
-  if (same) {
-    if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, b_box_rows(pair)))) return rc;
+  ps::GemmArgs a = base_args(n, n, n, L);
+  if (pair) {
+    if ((rc = map_pair_operand(&ta, p, false, n, n, L, n, n * n, &a.a_chunk))) return rc;
+    if ((rc = map_pair_operand(&tb, q, !same, n, n, L, n, n * n, &a.b_chunk))) return rc;
   } else {
-    if ((rc = map_mnmajor(&tb, q, n, n, L, n, n * n))) return rc;
+    if ((rc = map_kmajor(&ta, p, n, n, L, n, n * n, ps::BM))) return rc;
+    if (same) {
+      if ((rc = map_kmajor(&tb, q, n, n, L, n, n * n, b_box_rows(pair)))) return rc;
+    } else {
+      if ((rc = map_mnmajor(&tb, q, n, n, L, n, n * n))) return rc;
+    }
   }
   if ((rc = map_out(&td, out, PS_F16, n, n, L, n, n * n))) return rc;
-  ps::GemmArgs a = base_args(n, n, n, L);
   fill_sym_tiles(a, n, L);
   a.alpha = alpha;
   a.beta = beta;
@@ -670,7 +713,12 @@ int sym_product_impl(const void* p, const void* q, const void* c, void* out, int
   if (same && tri) {
     // squared operand and result both held as upper-triangle blocks
     CUtensorMap tm;
-    if ((rc = map_mnmajor(&tm, p, n, n, L, n, n * n))) return rc;
+    if (pair) {
+      if ((rc = map_pair_operand(&tm, p, true, n, n, L, n, n * n, &a.a2_chunk))) return rc;
+      a.b2_chunk = a.a2_chunk;
+    } else if ((rc = map_mnmajor(&tm, p, n, n, L, n, n * n))) {
+      return rc;
+    }
     a.a_tri = a.b_tri = 1;
     a.store_mirror = 0;
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfSquare,
@@ -702,13 +750,26 @@ int gram_impl(const void* x, void* out, int64_t L, int64_t rows, int64_t cols, i
   const double flops = static_cast<double>(L) * n * n * K;
   const double bytes = static_cast<double>(L) * 2.0 * (static_cast<double>(n) * K + n * n);
   const bool pair = use_pair(false, n);
+  // both operands read through one map: diagonal pair tiles stage their rows once
+  a.same_ab = pair ? 1 : 0;
   if (!tall) {
-    if ((rc = map_kmajor(&ta, x, K, n, L, x_ld, rows * x_ld, ps::BM))) return rc;
-    if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, b_box_rows(pair)))) return rc;
+    if (pair) {
+      if ((rc = map_pair_operand(&ta, x, false, K, n, L, x_ld, rows * x_ld, &a.a_chunk))) return rc;
+      tb = ta;
+      a.b_chunk = a.a_chunk;
+    } else {
+      if ((rc = map_kmajor(&ta, x, K, n, L, x_ld, rows * x_ld, ps::BM))) return rc;
+      if ((rc = map_kmajor(&tb, x, K, n, L, x_ld, rows * x_ld, b_box_rows(pair)))) return rc;
+    }
     return launch_gemm<false, false, true, ps::kOutF16>(0, ta, tb, td, a, stream, kProfGram,
                                                         flops, bytes, pair);
   }
-  if ((rc = map_mnmajor(&ta, x, n, K, L, x_ld, rows * x_ld))) return rc;
+  if (pair) {
+    if ((rc = map_pair_operand(&ta, x, true, n, K, L, x_ld, rows * x_ld, &a.a_chunk))) return rc;
+    a.b_chunk = a.a_chunk;
+  } else if ((rc = map_mnmajor(&ta, x, n, K, L, x_ld, rows * x_ld))) {
+    return rc;
+  }
   return launch_gemm<true, true, true, ps::kOutF16>(1, ta, ta, td, a, stream, kProfGram, flops,
                                                     bytes, pair);
 }
@@ -743,8 +804,18 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
   CUtensorMap ta, tb, td;
   int rc;
   const int64_t M = tall ? m : n, N = tall ? n : m;
+  const bool pair = use_pair(false, n);
+  ps::GemmArgs a = base_args(M, N, n, L);
   if ((rc = map_out(&td, y, y_dtype, N, M, L, y_ld, rows * y_ld))) return rc;
-  if (!tall) {
+  if (pair) {
+    if (!tall) {
+      if ((rc = map_pair_operand(&ta, b, false, n, n, L, n, n * n, &a.a_chunk))) return rc;
+      if ((rc = map_pair_operand(&tb, x, true, m, n, L, x_ld, rows * x_ld, &a.b_chunk))) return rc;
+    } else {
+      if ((rc = map_pair_operand(&ta, x, false, n, m, L, x_ld, rows * x_ld, &a.a_chunk))) return rc;
+      if ((rc = map_pair_operand(&tb, b, true, n, n, L, n, n * n, &a.b_chunk))) return rc;
+    }
+  } else if (!tall) {
     if ((rc = map_kmajor(&ta, b, n, n, L, n, n * n, ps::BM))) return rc;
     if ((rc = map_mnmajor(&tb, x, m, n, L, x_ld, rows * x_ld))) return rc;
   } else {
@@ -752,7 +823,6 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
     if ((rc = map_kmajor(&ta, x, n, m, L, x_ld, rows * x_ld, ps::BM))) return rc;
     if ((rc = map_mnmajor(&tb, b, n, n, L, n, n * n))) return rc;
   }
-  ps::GemmArgs a = base_args(M, N, n, L);
   fill_gen_tiles(a, M, N, L);
   if (residual != 0.f) {
     a.has_addend = 1;
@@ -765,20 +835,28 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
   CUtensorMap t2;
   if (tri_b) {
     if (!tall) {
-      if ((rc = map_mnmajor(&t2, b, n, n, L, n, n * n))) return rc;
+      if (pair) {
+        if ((rc = map_pair_operand(&t2, b, true, n, n, L, n, n * n, &a.a2_chunk))) return rc;
+      } else if ((rc = map_mnmajor(&t2, b, n, n, L, n, n * n))) {
+        return rc;
+      }
       a.a_tri = 1;
     } else {
-      if ((rc = map_kmajor(&t2, b, n, n, L, n, n * n, b_box_rows(use_pair(false, n))))) return rc;
+      if (pair) {
+        if ((rc = map_pair_operand(&t2, b, false, n, n, L, n, n * n, &a.b2_chunk))) return rc;
+      } else if ((rc = map_kmajor(&t2, b, n, n, L, n, n * n, b_box_rows(false)))) {
+        return rc;
+      }
       a.b_tri = 1;
     }
   }
   switch (y_dtype) {
     case PS_F16:
-      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream, &t2, use_pair(false, n));
+      return apply_launch<ps::kOutF16>(tall, ta, tb, td, a, stream, &t2, pair);
     case PS_F32:
-      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream, &t2, use_pair(false, n));
+      return apply_launch<ps::kOutF32>(tall, ta, tb, td, a, stream, &t2, pair);
     default:
-      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream, &t2, use_pair(false, n));
+      return apply_launch<ps::kOutBF16>(tall, ta, tb, td, a, stream, &t2, pair);
   }
 }
 

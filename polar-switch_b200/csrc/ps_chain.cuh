@@ -44,8 +44,8 @@ struct Step {
 };
 
 struct alignas(64) ChainParams {
-  CUtensorMap tmK[MAX_BUFS];   // K-major operand boxes, 64 (K) x 128 rows
-  CUtensorMap tmMN[MAX_BUFS];  // MN-major boxes, 64 x 64: blocks read transposed
+  CUtensorMap tmK[MAX_BUFS];   // K-major operand stages (see pair::load_operand)
+  CUtensorMap tmMN[MAX_BUFS];  // MN-major operand stages: blocks read transposed
   CUtensorMap tmD[MAX_BUFS];   // 32 x 32 output boxes
   const __half* buf[MAX_BUFS]; // buffer bases: L stacked n x n matrices each
   Step steps[MAX_STEPS];
@@ -54,6 +54,7 @@ struct alignas(64) ChainParams {
   int chunk;                   // matrices per chunk
   int n_items, total_tiles;
   int nbufs;
+  int chunked;                 // tmK / tmMN are 4-D chunked maps (n % 64 == 0)
   unsigned base;               // counter value at the start of this launch
   unsigned* done;              // per-matrix completion counters
   int* status;
@@ -105,7 +106,6 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
   using pair::STAGE_BYTES;
   using pair::STAGES;
   using pair::TMEM_COLS;
-  using pair::UMMA_K;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -202,22 +202,9 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
           const int k0 = kb * BK;
           const bool at = tri_transposed(false, a_lo, a_lo + 1, k0 / BM);
           const bool bt = tri_transposed(false, b_lo, b_lo + 1, k0 / BM);
-          if (!at) {
-            tma_load_3d_pair(mk, a_dst, bar, k0, m0, b);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j)
-              tma_load_3d_pair(mmn, a_dst + j * MN_ATOM_BYTES, bar, m0 + 64 * j, k0, b);
-          }
-          if (share) {
-            // B half == A block: nothing more to load
-          } else if (!bt) {
-            tma_load_3d_pair(mk, b_dst, bar, k0, nb, b);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BNH / 64; ++j)
-              tma_load_3d_pair(mmn, b_dst + j * MN_ATOM_BYTES, bar, nb + 64 * j, k0, b);
-          }
+          pair::load_operand(at ? mmn : mk, P.chunked != 0, at, a_dst, bar, m0, k0, b);
+          if (!share)  // diagonal pair tile: B half == A block
+            pair::load_operand(bt ? mmn : mk, P.chunked != 0, bt, b_dst, bar, nb, k0, b);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -251,6 +238,8 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
       bool issued_any = false;
       const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), peer);
       const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), peer);
+      const uint32_t smem_base = smem_u32(smem);
+      const uint32_t idesc0 = make_idesc_f16(2 * BM, BN, false, false);
       for (int t = pair_id; t < P.total_tiles && ok; t += npairs) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, P.status,
                                kStatusMmaTimeout, P.wait_limit)) {
@@ -270,22 +259,11 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t a_addr = smem_base + stage * STAGE_BYTES;
           const uint32_t b_addr = share ? a_addr : a_addr + A_STAGE_BYTES;
           const int kb128 = (kb * BK) / BM;
-          const bool a_mn = tri_transposed(false, a_lo, a_lo + 1, kb128);
-          const bool b_mn = tri_transposed(false, b_lo, b_lo + 1, kb128);
-          const uint32_t idesc = make_idesc_f16(2 * BM, BN, a_mn, b_mn);
-#pragma unroll
-          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint64_t ad = a_mn ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
-                                                            MN_ATOM_BYTES, 1024)
-                                     : make_smem_desc_sw128(a_addr + kk * (UMMA_K * 2), 16, 1024);
-            const uint64_t bd = b_mn ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
-                                                            MN_ATOM_BYTES, 1024)
-                                     : make_smem_desc_sw128(b_addr + kk * (UMMA_K * 2), 16, 1024);
-            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
-          }
+          pair::mma_stage(d_tmem, a_addr, b_addr, tri_transposed(false, a_lo, a_lo + 1, kb128),
+                          tri_transposed(false, b_lo, b_lo + 1, kb128), idesc0, kb == 0);
           issued_any = true;
           umma_commit_pair(smem_u32(&empty[stage]));
           umma_commit_pair(empty_peer0 + stage * 8);

@@ -74,6 +74,9 @@ struct GemmArgs {
   // Symmetric A . A^T with both operands read through identical maps: the
   // CTA-pair kernel then stages a diagonal pair tile's rows once.
   int same_ab;
+  // CTA-pair path only: the operand map is a 4-D chunked map (one TMA per
+  // 128-wide K stage, see ps_gemm2.cuh); the one-CTA kernel ignores these.
+  int a_chunk, b_chunk, a2_chunk, b2_chunk;
   int* status;               // device status word
   long long wait_limit;      // cycles before a bounded wait gives up
 };

@@ -46,21 +46,80 @@ namespace pair {
 constexpr int BM = 128;                 // rows per CTA
 constexpr int BN = 256;                 // accumulator columns per CTA (pair N)
 constexpr int BNH = 128;                // B columns staged per CTA
-constexpr int BK = 64;
-constexpr int STAGES = 5;
+constexpr int BK = 128;                 // K per stage: two 64-wide (128-byte) sub-blocks
+constexpr int STAGES = 3;
 constexpr int UMMA_K = 16;
-constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB
-constexpr int B_STAGE_BYTES = BNH * BK * 2;  // 16 KB
+constexpr int SLAB_BYTES = 128 * 64 * 2;       // 16 KB: 128 rows (or K) x 64 halves
+constexpr int A_STAGE_BYTES = BM * BK * 2;     // 32 KB
+constexpr int B_STAGE_BYTES = BNH * BK * 2;    // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;  // 320
-constexpr int EPI_WARP_BYTES = 8192;
+constexpr int EPI_WARP_BYTES = 4096;
 constexpr int SMEM_OPERANDS = STAGES * STAGE_BYTES;
 constexpr int SMEM_EPI = NUM_EPI_WARPS * EPI_WARP_BYTES;
 constexpr int SMEM_CTRL = 256;
 constexpr int SMEM_TOTAL = SMEM_OPERANDS + SMEM_EPI + SMEM_CTRL + 1024;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 static_assert(SMEM_TOTAL <= 232448, "shared memory budget");
+
+// One operand stage: 128 rows (or columns) of the operand by 128 of K, in
+// two 16 KB slabs with 128-byte swizzle:
+//   K-major : slab h = K sub-block h, [row 0..127][64 halves of K]
+//   MN-major: slab j = 64-wide M/N half j, [k 0..127][64 halves of M/N]
+// A "chunked" map (4-D: 64 | rows or K | 64-chunks | L) fills a stage with
+// one TMA; a plain 3-D map takes two boxes (K-major) or four (MN-major). The
+// per-instruction cost of a CTA-pair TMA, not its size, limits the operand
+// stream, hence the large boxes.
+__device__ __forceinline__ void load_operand(const CUtensorMap* map, bool chunked, bool mn_major,
+                                             uint8_t* dst, uint32_t bar, int r0, int k0, int b) {
+  if (!mn_major) {
+    if (chunked) {
+      tma_load_4d_pair(map, dst, bar, 0, r0, k0 / 64, b);
+    } else {
+      tma_load_3d_pair(map, dst, bar, k0, r0, b);
+      tma_load_3d_pair(map, dst + SLAB_BYTES, bar, k0 + 64, r0, b);
+    }
+  } else {
+    if (chunked) {
+      tma_load_4d_pair(map, dst, bar, 0, k0, r0 / 64, b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d_pair(map, dst + j * SLAB_BYTES + h * (SLAB_BYTES / 2), bar, r0 + 64 * j,
+                           k0 + 64 * h, b);
+    }
+  }
+}
+
+// Shared-memory descriptor pieces (tcgen05 format, 128-byte swizzle): the
+// high word (stride between 8-row groups 1024 B, version 1, swizzle mode) is
+// fixed; the low word holds the leading-byte offset and the start address.
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+constexpr uint32_t kDescLoK = (16u >> 4) << 16;                               // K-major
+constexpr uint32_t kDescLoMN = (static_cast<uint32_t>(SLAB_BYTES) >> 4) << 16;  // MN halves 16 KB apart
+
+// The 8 UMMAs (2 sub-blocks x 4 of K = 16) of one stage.
+__device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr,
+                                          bool a_mn, bool b_mn, uint32_t idesc0, bool first) {
+  const uint32_t idesc = idesc0 | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u);
+  const uint32_t alo = (a_mn ? kDescLoMN : kDescLoK) | (a_addr >> 4);
+  const uint32_t blo = (b_mn ? kDescLoMN : kDescLoK) | (b_addr >> 4);
+  // per sub-block: MN-major 64 K-rows (8 KB), K-major one 16 KB slab; per
+  // UMMA_K step: MN-major 16 K-rows (2 KB), K-major 32 bytes (>> 4 below)
+  const uint32_t a_sub = a_mn ? 512u : 1024u, b_sub = b_mn ? 512u : 1024u;
+  const uint32_t a_kk = a_mn ? 128u : 2u, b_kk = b_mn ? 128u : 2u;
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint64_t ad = (static_cast<uint64_t>(kDescHi) << 32) | (alo + h * a_sub + kk * a_kk);
+      const uint64_t bd = (static_cast<uint64_t>(kDescHi) << 32) | (blo + h * b_sub + kk * b_kk);
+      umma_f16_pair(d_tmem, ad, bd, idesc, (first && h == 0 && kk == 0) ? 0u : 1u);
+    }
+}
 
 struct PairArgs {
   int M, N, K, L;
@@ -75,6 +134,7 @@ struct PairArgs {
   int a_tri, b_tri;       // operand stored as upper-triangle blocks only
   int store_mirror;       // symmetric: also store the transposed off-diagonal blocks
   int same_ab;            // symmetric A . A^T, A and B maps identical (see below)
+  int a_chunk, b_chunk, a2_chunk, b2_chunk;  // map is 4-D chunked (one TMA per stage)
   int* status;
   long long wait_limit;
 };
@@ -194,24 +254,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int k0 = kb * BK;
           const bool at = args.a_tri && tri_transposed(A_MN, a_lo, a_lo + 1, k0 / BM);
           const bool bt = args.b_tri && tri_transposed(B_MN, b_lo, b_lo + 1, k0 / BM);
-          const CUtensorMap* ma = at ? &tmA2 : &tmA;
-          const CUtensorMap* mb = bt ? &tmB2 : &tmB;
-          if (A_MN == at) {  // K-major tile
-            tma_load_3d_pair(ma, a_dst, bar, k0, m0, b);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j)
-              tma_load_3d_pair(ma, a_dst + j * MN_ATOM_BYTES, bar, m0 + 64 * j, k0, b);
-          }
-          if (share) {
-            // B half == A block: nothing more to load
-          } else if (B_MN == bt) {
-            tma_load_3d_pair(mb, b_dst, bar, k0, nb, b);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BNH / 64; ++j)
-              tma_load_3d_pair(mb, b_dst + j * MN_ATOM_BYTES, bar, nb + 64 * j, k0, b);
-          }
+          load_operand(at ? &tmA2 : &tmA, (at ? args.a2_chunk : args.a_chunk) != 0, A_MN != at, a_dst,
+                       bar, m0, k0, b);
+          if (!share)  // a shared diagonal tile's B half is its A block: nothing more to load
+            load_operand(bt ? &tmB2 : &tmB, (bt ? args.b2_chunk : args.b_chunk) != 0, B_MN != bt,
+                         b_dst, bar, nb, k0, b);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -247,6 +294,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
       const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), peer);
       const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), peer);
+      const uint32_t smem_base = smem_u32(smem);
+      const uint32_t idesc0 = make_idesc_f16(2 * BM, BN, false, false);
       for (int t = pair_id; t < args.total_tiles && ok; t += npairs) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status,
                                kStatusMmaTimeout, args.wait_limit)) {
@@ -266,22 +315,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t a_addr = smem_base + stage * STAGE_BYTES;
           const uint32_t b_addr = share ? a_addr : a_addr + A_STAGE_BYTES;
           const int kb128 = (kb * BK) / BM;
           const bool a_mn = A_MN != (args.a_tri && tri_transposed(A_MN, a_lo, a_lo + 1, kb128));
           const bool b_mn = B_MN != (args.b_tri && tri_transposed(B_MN, b_lo, b_lo + 1, kb128));
-          const uint32_t idesc = make_idesc_f16(2 * BM, BN, a_mn, b_mn);
-#pragma unroll
-          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint64_t ad = a_mn ? make_smem_desc_sw128(a_addr + kk * (UMMA_K * 128),
-                                                            MN_ATOM_BYTES, 1024)
-                                     : make_smem_desc_sw128(a_addr + kk * (UMMA_K * 2), 16, 1024);
-            const uint64_t bd = b_mn ? make_smem_desc_sw128(b_addr + kk * (UMMA_K * 128),
-                                                            MN_ATOM_BYTES, 1024)
-                                     : make_smem_desc_sw128(b_addr + kk * (UMMA_K * 2), 16, 1024);
-            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
-          }
+          mma_stage(d_tmem, a_addr, b_addr, a_mn, b_mn, idesc0, kb == 0);
           issued_any = true;
           // free this stage in both CTAs
           umma_commit_pair(smem_u32(&empty[stage]));

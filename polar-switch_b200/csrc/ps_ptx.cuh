@@ -283,6 +283,17 @@ __device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, void* s
       : "memory");
 }
 
+// 4-D form of tma_load_3d_pair (one box over a "chunked" view of a matrix).
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, void* smem_dst,
+                                                 uint32_t bar_cluster, int c0, int c1, int c2,
+                                                 int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(dst_smem)),

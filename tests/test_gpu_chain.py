@@ -82,7 +82,7 @@ def test_chain_single_call_and_more_steps_than_one_launch(cuda_device):
 
 
 @pytest.mark.parametrize("method,shape", [("PS3_55", (2, 1152, 2304)), ("PS2_55", (1, 2048, 2048)),
-                                          ("PS2_55", (3, 1024, 1536))])
+                                          ("PS2_55", (3, 1024, 1536)), ("PS3_55", (2, 1088, 1088))])
 def test_chain_on_pairs_for_larger_n(cuda_device, method, shape):
     """With every product on CTA pairs (ps_set_cta_pairs(1)) the chain also
     takes n > 1024 (more pair tiles per matrix, a ragged last pair block)."""

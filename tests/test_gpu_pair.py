@@ -1,7 +1,10 @@
 """The CTA-pair GEMM kernel (tcgen05 cta_group::2, 256 x 256 tiles) against
 the one-CTA kernel and the oracle, on shapes that exercise its tile edges:
 odd numbers of 128-row blocks (the last column pair and row pair half out of
-range), partial blocks, tall and wide operands, and batches."""
+range), partial blocks, tall and wide operands, and batches. Sizes that are
+multiples of 64 load each 128-wide K stage with one TMA over a 4-D chunked
+view (1088 = 17 x 64: the last stage half out of range), other sizes with
+two or four 3-D boxes; both fill the same shared-memory layout."""
 
 import pytest
 import torch
@@ -30,7 +33,8 @@ def _both(fn):
     return a, b
 
 
-@pytest.mark.parametrize("L,n", [(1, 128), (2, 256), (1, 384), (3, 136), (1, 1152), (2, 640), (1, 8)])
+@pytest.mark.parametrize("L,n", [(1, 128), (2, 256), (1, 384), (3, 136), (1, 1152), (2, 640), (1, 8),
+                                 (1, 1088), (2, 192)])
 def test_square_pair_vs_single(cuda_device, L, n):
     from polar_switch import cuda_ops
     A = _sym(n, L, 300 + n).to(cuda_device)
@@ -47,7 +51,8 @@ def test_square_pair_vs_single(cuda_device, L, n):
     assert torch.equal(pair, pair.mT)
 
 
-@pytest.mark.parametrize("L,rows,cols", [(2, 384, 1024), (1, 1152, 1000), (3, 520, 136), (1, 96, 200)])
+@pytest.mark.parametrize("L,rows,cols", [(2, 384, 1024), (1, 1152, 1000), (3, 520, 136), (1, 96, 200),
+                                         (1, 1088, 2112), (2, 2112, 1088), (1, 320, 192)])
 def test_gram_pair_vs_single(cuda_device, L, rows, cols):
     from polar_switch import cuda_ops
     X = oc.normalize(seeded((L, rows, cols), 310 + rows), 1e-7).to(cuda_device)
@@ -64,7 +69,7 @@ def test_gram_pair_vs_single(cuda_device, L, rows, cols):
 
 
 @pytest.mark.parametrize("L,rows,cols", [(2, 256, 1024), (1, 1152, 384), (3, 200, 96), (1, 136, 520),
-                                         (2, 640, 2048)])
+                                         (2, 640, 2048), (1, 1088, 2112), (1, 2112, 1088)])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 def test_apply_pair_vs_single(cuda_device, L, rows, cols, out_dtype):
     from polar_switch import cuda_ops
@@ -100,7 +105,8 @@ def test_circuit_pair_vs_single(cuda_device):
 
 
 @pytest.mark.parametrize("method,shape", [("PS2_55", (2, 384, 1152)), ("PS3_55", (1152, 640)),
-                                          ("POLAR_EXPRESS", (3, 256, 384)), ("PS2_55", (1, 200, 72))])
+                                          ("POLAR_EXPRESS", (3, 256, 384)), ("PS2_55", (1, 200, 72)),
+                                          ("PS3_55", (1, 1088, 2176))])
 def test_triangle_storage_circuit_is_bit_identical(cuda_device, method, shape):
     """Inside a circuit the square buffers are kept as upper-triangle blocks and
     read back transposed; the result must equal, bit for bit, the op-by-op
