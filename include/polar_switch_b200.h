@@ -119,14 +119,15 @@ PS_API int ps_profile_read(int kind, double* total_ms, int64_t* launches, double
                            double* bytes);
 
 /* Selects the GEMM kernel for later launches: 0 = one-CTA kernel (128 x 256
- * tiles), 1 = CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles over two
- * SMs), 2 (default) = CTA pairs for squares of buffers with n <= 1024, the
- * one-CTA kernel for everything else. All compute the same products with the
- * same rounding. Returns the previous mode (PS_ERR_INVALID for other values). */
+ * tiles), 1 (default) = CTA-pair kernel (tcgen05 cta_group::2, 256 x 256
+ * tiles over two SMs) for every product, 2 = CTA pairs for squares of buffers
+ * with n <= 1024 and the one-CTA kernel for everything else. All compute the
+ * same products with the same rounding. Returns the previous mode
+ * (PS_ERR_INVALID for other values). */
 PS_API int ps_set_cta_pairs(int mode);
 
 /* How the inner iterations of ps_circuit / ps_circuit_grouped run on the
- * CTA-pair path (square buffers with n <= 1024): 1 (default) = one persistent
+ * CTA-pair path (every n under ps_set_cta_pairs(1)): 1 (default) = one persistent
  * launch per outer iteration for all of them ("chain": a step of a matrix
  * starts as soon as that matrix's previous step is stored, so its buffers are
  * reused from L2), 0 = one launch per inner iteration. Same bits either way.

@@ -54,14 +54,12 @@ enum ProfKind : int {
 
 thread_local std::string g_last_error;
 long long g_wait_limit = ps::kDefaultWaitLimit;
-// GEMMs run on the one-CTA kernel unless CTA pairs (cta_group::2) are selected
-// with ps_set_cta_pairs; measured faster on every circuit shape.
-// Which GEMM kernel runs: 0 = the one-CTA kernel, 1 = the CTA-pair kernel, 2
-// (default) = CTA pairs for squares of buffers up to kPairMaxN (where sharing
-// the B tile across the pair pays: measured 17 % faster at n = 1024), the
-// one-CTA kernel for everything else (Grams, applies and large squares run
-// faster there).
-int g_pair_mode = 2;
+// Which GEMM kernel runs: 0 = the one-CTA kernel, 1 (default) = the CTA-pair
+// kernel for every product, 2 = CTA pairs for squares of buffers up to
+// kPairMaxN and the one-CTA kernel for everything else. With whole 128-wide K
+// stages per TMA the pair kernel measured faster than or equal to mode 2 on
+// every BASELINE workload (Qwen step +4 %, 8192^2 circuit +8 %).
+int g_pair_mode = 1;
 constexpr int64_t kPairMaxN = 1024;
 // Upper bound on the CTAs (SMs) a persistent GEMM grid may take; 0 = all SMs.
 // Leaving SMs free lets a collective run beside the GEMMs.

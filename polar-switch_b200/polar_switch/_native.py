@@ -188,8 +188,9 @@ def profile_read():
 
 
 def set_cta_pairs(mode):
-    """GEMM kernel selection: 0/False one-CTA kernel, 1/True CTA pairs, 2 (default) CTA
-    pairs for squares with n <= 1024 only. Returns the previous mode (an int)."""
+    """GEMM kernel selection: 0/False one-CTA kernel, 1/True (default) CTA pairs for
+    every product, 2 CTA pairs for squares with n <= 1024 only. Returns the previous
+    mode (an int)."""
     rc = load().ps_set_cta_pairs(int(mode))
     if rc < 0:
         check("ps_set_cta_pairs", rc)

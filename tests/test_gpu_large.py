@@ -5,9 +5,9 @@ few percent of elements allowed to differ by that one rounding flip; where a
 square's epilogue cancels, the result may also differ by n * 2^-26 of the
 magnitude of its terms, the tensor cores' truncating FP32 accumulation over
 K = n -- see tests/_util.assert_fp16_close):
-  * symmetric products with more than 16 row blocks of 128 (n > 2048), whose
-    tiles are visited in bands (the banded tile decoder), on the one-CTA
-    kernel and on CTA pairs;
+  * symmetric products with more than 16 row blocks of 128 (n > 2048), on CTA
+    pairs and on the one-CTA kernel (whose tiles are then visited in bands,
+    the banded tile decoder);
   * the one-CTA square at n = 2048 (16 row blocks, plain row order);
   * wide and tall Grams with long K (m = 2n) at n = 2304 and 4096.
 
@@ -39,14 +39,15 @@ SIGMA_TOL = 1e-3
 SIGMA_TOL_PS3 = 2e-3
 
 
-@pytest.fixture(params=["default", "pairs"])
+@pytest.fixture(params=["default", "onecta"])
 def kernel_mode(request):
-    """Run a test on the default kernel choice, then with every product on CTA pairs."""
+    """Run a test on the default kernel (CTA pairs), then on the one-CTA kernel,
+    whose symmetric tiles above 16 row blocks go through the banded decoder."""
     from polar_switch import _native as nat
     if request.param == "default":
         yield request.param
         return
-    prev = nat.set_cta_pairs(1)
+    prev = nat.set_cta_pairs(0)
     try:
         yield request.param
     finally:

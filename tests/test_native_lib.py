@@ -71,9 +71,9 @@ def test_host_side_knobs_round_trip_without_gpu():
     lib = _native.load()
     assert lib.ps_set_cta_pairs(3) == _native.PS_ERR_INVALID
     assert lib.ps_set_cta_pairs(-1) == _native.PS_ERR_INVALID
-    prev = lib.ps_set_cta_pairs(1)
-    assert prev == 2  # default: pairs for small squares only
-    assert lib.ps_set_cta_pairs(0) == 1
+    prev = lib.ps_set_cta_pairs(2)
+    assert prev == 1  # default: CTA pairs for every product
+    assert lib.ps_set_cta_pairs(0) == 2
     assert lib.ps_set_cta_pairs(prev) == 0
     assert lib.ps_set_max_ctas(-5) == _native.PS_ERR_INVALID
     assert lib.ps_set_max_ctas(100) == 0
