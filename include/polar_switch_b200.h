@@ -136,6 +136,15 @@ PS_API int ps_set_cta_pairs(int mode);
  * kernel per inner iteration). */
 PS_API int ps_set_chain(int mode);
 
+/* How ps_circuit / ps_circuit_grouped normalise contiguous, unpadded inputs:
+ * 1 = one read of the input (a persistent kernel keeps each chunk in shared
+ * memory until its matrix's norm is known), 0 (default) = two passes over the
+ * input (sums of squares, then scale and cast). Same bits either way; the
+ * single read measured slower than the two passes at the Qwen step. Returns
+ * the previous mode (PS_ERR_INVALID for other values). No counterpart in the
+ * reference (polar_switch/__init__.py:34-35 normalises in two torch ops). */
+PS_API int ps_set_fused_normalize(int mode);
+
 /* Caps the number of CTAs (one per SM) of the persistent GEMM grids launched
  * afterwards; 0 (default) = every SM. Leaving SMs free lets a collective on
  * another stream run beside the GEMMs. Returns the previous cap. */

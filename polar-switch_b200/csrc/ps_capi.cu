@@ -68,6 +68,12 @@ int g_max_ctas = 0;
 // persistent chain launch per outer iteration (1, default) or one launch per
 // inner iteration (0). Both give the same bits.
 int g_chain_mode = 1;
+// Normalisations of grouped circuits read each contiguous input once (the
+// fused single-read kernel) when 1, or run the two passes when 0 (default).
+// Both give the same bits; the single read measured slower on the Qwen step
+// (2.7 against 6.2 TB/s of algorithmic traffic: CTAs holding chunks wait for
+// the rest of their matrix in waves), so it is off until that is fixed.
+int g_norm_fused = 0;
 
 // Every kernel launch of the library is counted; when profiling is enabled,
 // each launch is also bracketed by CUDA events on its stream and tagged with
@@ -144,6 +150,7 @@ struct DeviceState {
   int pair_clusters[kNumVariants] = {};
   bool chain_ready = false;
   int chain_clusters = 0;
+  int norm_fused_grid[4] = {};  // resident CTAs of the fused normalisation, by dtype
 };
 
 std::mutex g_mu;
@@ -1011,7 +1018,72 @@ struct NormJob {
   void* xh;
   int64_t Rp, Cp;
   double* partial;
+  unsigned* count;  // L zeroed counters for the fused kernel (nullptr: two passes)
 };
+
+// Resident CTAs of the fused normalisation for input type T on this device
+// (one NORM_CHUNK chunk of T in shared memory per CTA); 0 if it cannot run.
+template <typename T>
+int norm_fused_grid(DeviceState* st, int dtype) {
+  if (st->norm_fused_grid[dtype]) return st->norm_fused_grid[dtype];
+  auto kern = ps::ps_normalize_fused_kernel<T>;
+  const int smem = ps::NORM_CHUNK * static_cast<int>(sizeof(T));
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, ps::NORM_THREADS, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  st->norm_fused_grid[dtype] = per_sm * st->sms;
+  return st->norm_fused_grid[dtype];
+}
+
+// Whether a job can take the fused kernel: contiguous, unpadded, aligned, and
+// every matrix's chunks (of NORM_CHUNK elements) fit in the resident grid.
+bool norm_fused_ok(const NormJob& j, int grid, int elem) {
+  const int64_t E = j.R * j.C;
+  const int64_t nch = (E + ps::NORM_CHUNK - 1) / ps::NORM_CHUNK;
+  return g_norm_fused && j.count && grid > 0 && j.sC == 1 && j.sR == j.C && j.sL == E &&
+         j.Rp == j.R && j.Cp == j.C && E % 8 == 0 && (E * elem) % 16 == 0 && aligned16(j.x) &&
+         aligned16(j.xh) && nch <= ps::NORM_MAX_CHUNKS && nch <= grid;
+}
+
+template <typename T>
+int launch_normalize_fused(const NormJob* jobs, int n, float eps, DeviceState* st, int grid,
+                           cudaStream_t s) {
+  ps::NormFused f;
+  std::memset(&f, 0, sizeof(f));
+  f.count = n;
+  f.eps = eps;
+  f.status = st->status;
+  f.wait_limit = g_wait_limit;
+  long long t = 0;
+  double elems = 0.0;
+  for (int i = 0; i < n; ++i) {
+    const NormJob& j = jobs[i];
+    ps::NormFusedProblem& q = f.p[i];
+    q.x = j.x;
+    q.xh = static_cast<__half*>(j.xh);
+    q.partial = j.partial;
+    q.count = j.count;
+    q.E = j.R * j.C;
+    q.chunks = static_cast<int>((q.E + ps::NORM_CHUNK - 1) / ps::NORM_CHUNK);
+    q.t0 = t;
+    t += j.L * q.chunks;
+    elems += static_cast<double>(j.L) * q.E;
+  }
+  f.total = t;
+  const int g = static_cast<int>(t < grid ? t : grid);
+  LaunchScope scope(kProfNormalize, s, 3.0 * elems, elems * (sizeof(T) + 2.0));
+  ps::ps_normalize_fused_kernel<T>
+      <<<g, ps::NORM_THREADS, ps::NORM_CHUNK * sizeof(T), s>>>(f);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "fused normalize launch");
+}
+
 
 // Both passes of up to NORM_BATCH_MAX normalisations with input type T, one
 // launch per pass. Each matrix keeps normalize_impl's chunk count and chunk
@@ -1089,10 +1161,37 @@ int normalize_jobs(const std::vector<NormJob>& jobs, float eps, int sms, cudaStr
   if (!(eps > 0.f)) return fail(PS_ERR_INVALID, "ps_normalize: eps must be positive");
   for (const NormJob& j : jobs)
     if (elem_bytes(j.x_dtype) == 0) return fail(PS_ERR_INVALID, "ps_normalize: bad dtype");
+  DeviceState* st = nullptr;
+  int rc0 = device_state(&st);
+  if (rc0) return rc0;
   for (int dt : {PS_F16, PS_BF16, PS_F32, PS_F64}) {
-    std::vector<NormJob> same;
-    for (const NormJob& j : jobs)
-      if (j.x_dtype == dt) same.push_back(j);
+    int grid = 0;
+    switch (dt) {
+      case PS_F16: grid = norm_fused_grid<__half>(st, dt); break;
+      case PS_BF16: grid = norm_fused_grid<__nv_bfloat16>(st, dt); break;
+      case PS_F32: grid = norm_fused_grid<float>(st, dt); break;
+      default: grid = norm_fused_grid<double>(st, dt); break;
+    }
+    std::vector<NormJob> same, fused;
+    for (const NormJob& j : jobs) {
+      if (j.x_dtype != dt) continue;
+      if (norm_fused_ok(j, grid, elem_bytes(dt)))
+        fused.push_back(j);
+      else
+        same.push_back(j);
+    }
+    for (size_t i0 = 0; i0 < fused.size(); i0 += ps::NORM_BATCH_MAX) {
+      const int n = static_cast<int>(std::min<size_t>(fused.size() - i0, ps::NORM_BATCH_MAX));
+      const NormJob* b = fused.data() + i0;
+      int rc;
+      switch (dt) {
+        case PS_F16: rc = launch_normalize_fused<__half>(b, n, eps, st, grid, s); break;
+        case PS_BF16: rc = launch_normalize_fused<__nv_bfloat16>(b, n, eps, st, grid, s); break;
+        case PS_F32: rc = launch_normalize_fused<float>(b, n, eps, st, grid, s); break;
+        default: rc = launch_normalize_fused<double>(b, n, eps, st, grid, s); break;
+      }
+      if (rc) return rc;
+    }
     for (size_t i0 = 0; i0 < same.size(); i0 += ps::NORM_BATCH_MAX) {
       const int n = static_cast<int>(std::min<size_t>(same.size() - i0, ps::NORM_BATCH_MAX));
       const NormJob* b = same.data() + i0;
@@ -1198,6 +1297,7 @@ struct GroupedPlan {
     int64_t goff;          // first matrix of this problem inside its n-group
     int64_t xh_off[2];
     int64_t norm_off;
+    int64_t cnt_off;  // L counters of the fused normalisation
   };
   struct NGroup {
     int64_t n, Ltot, buf_off, buf_bytes;
@@ -1248,6 +1348,10 @@ int make_grouped_plan(const ps_problem* probs, int n_probs, int buffers, int sms
   for (GroupedPlan::NGroup& g : plan->groups) {
     g.ctr_off = off;
     off += round_up(g.Ltot * static_cast<int64_t>(sizeof(unsigned)), 256);
+  }
+  for (int i = 0; i < n_probs; ++i) {
+    plan->probs[i].cnt_off = off;
+    off += round_up(probs[i].L * static_cast<int64_t>(sizeof(unsigned)), 256);
   }
   plan->ctr_bytes = off - plan->ctr_off;
   plan->total = off;
@@ -1434,6 +1538,14 @@ int ps_set_cta_pairs(int mode) {
   if (mode < 0 || mode > 2) return fail(PS_ERR_INVALID, "ps_set_cta_pairs: mode must be 0, 1 or 2");
   const int previous = g_pair_mode;
   g_pair_mode = mode;
+  return previous;
+}
+
+int ps_set_fused_normalize(int mode) {
+  if (mode < 0 || mode > 1)
+    return fail(PS_ERR_INVALID, "ps_set_fused_normalize: mode must be 0 or 1");
+  const int previous = g_norm_fused;
+  g_norm_fused = mode;
   return previous;
 }
 
@@ -1762,7 +1874,14 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
     const ps_problem& q = probs[i];
     const GroupedPlan::Prob& p = plan.probs[i];
     norm_jobs[i] = {q.x, q.x_dtype, q.L, q.rows, q.cols, q.sL, q.sR, q.sC, ws + p.xh_off[0],
-                    p.lay.Rp, p.lay.Cp, reinterpret_cast<double*>(ws + p.norm_off)};
+                    p.lay.Rp, p.lay.Cp, reinterpret_cast<double*>(ws + p.norm_off),
+                    reinterpret_cast<unsigned*>(ws + p.cnt_off)};
+  }
+  std::vector<unsigned> chain_base(plan.groups.size(), 0u);
+  {
+    // chain and fused-normalisation counters start at zero in every call
+    cudaError_t e = cudaMemsetAsync(ws + plan.ctr_off, 0, plan.ctr_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "counters memset");
   }
   // The normalisations of all problems, batched by input type.
   if ((rc = normalize_jobs(norm_jobs, eps, st->sms, s))) return rc;
@@ -1775,13 +1894,6 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
                 (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 && aligned16(q.y);
   }
   // Chain launches count completed tiles per matrix from zero within this call.
-  std::vector<unsigned> chain_base(plan.groups.size(), 0u);
-  bool any_chain = false;
-  for (const GroupedPlan::NGroup& g : plan.groups) any_chain |= use_chain(g.n, buffers);
-  if (any_chain) {
-    cudaError_t e = cudaMemsetAsync(ws + plan.ctr_off, 0, plan.ctr_bytes, s);
-    if (e != cudaSuccess) return cuda_fail(e, "chain counters memset");
-  }
   int off = 0;
   for (int t = 0; t < n_outer; ++t) {
     // The Grams of all problems, batched into one launch per kernel variant.

@@ -360,6 +360,135 @@ __global__ void __launch_bounds__(NORM_THREADS)
                   b.eps, q.xh, q.Rp, q.Cp, local / q.per, local % q.per, q.per);
 }
 
+// Both passes of the normalisation with one read of the input ("fused"), for
+// contiguous matrices without padding. A persistent grid walks the chunks of
+// all problems in order; a CTA loads its chunk into shared memory while
+// summing its squares exactly as ps_norm_partial_kernel does (same vectors per
+// thread, same FP32 order, same FP64 block tree), publishes the sum and bumps
+// its matrix's counter, waits (bounded) until every chunk of that matrix is
+// summed, forms the denominator as ps_scale_cast_kernel does (norm_den) and
+// writes its chunk's FP16 values from shared memory. So the bits are those of
+// the two-pass kernels, and the input crosses HBM once (6 instead of 10 bytes
+// per FP32 element).
+//
+// A CTA waits only for chunks of its own matrix, which sit at most
+// `chunks - 1` places after its own in the order; with every chunk count at
+// most the grid size and all CTAs resident, the earliest unfinished matrix
+// always has all its chunks held by running CTAs, so the waits end.
+struct NormFusedProblem {
+  const void* x;        // (L, E) contiguous input
+  __half* xh;           // (L, E) FP16 output
+  double* partial;      // L * chunks chunk sums
+  unsigned* count;      // L counters, zero on entry
+  long long E;          // elements per matrix
+  long long t0;         // first chunk of this problem in the launch
+  int chunks;           // chunks per matrix (chunk size NORM_CHUNK)
+};
+
+struct NormFused {
+  NormFusedProblem p[NORM_BATCH_MAX];
+  int count;
+  long long total;      // chunks of all problems
+  float eps;
+  int* status;
+  long long wait_limit;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(NORM_THREADS)
+    ps_normalize_fused_kernel(const __grid_constant__ NormFused F) {
+  extern __shared__ uint4 s_chunk[];  // NORM_CHUNK elements of T
+  __shared__ double s_warp[NORM_THREADS / 32];
+  __shared__ float s_den;
+  __shared__ int s_ok;
+  constexpr int VW = Vec16<T>::VW;
+  T* sdata = reinterpret_cast<T*>(s_chunk);
+  for (long long t = blockIdx.x; t < F.total; t += gridDim.x) {
+    int pi = 0;
+    while (pi + 1 < F.count && t >= F.p[pi + 1].t0) ++pi;
+    const NormFusedProblem& q = F.p[pi];
+    const long long local = t - q.t0;
+    const long long l = local / q.chunks, c = local - l * q.chunks;
+    const long long beg = c * NORM_CHUNK;
+    const long long n = q.E - beg < NORM_CHUNK ? q.E - beg : NORM_CHUNK;
+    const T* src = static_cast<const T*>(q.x) + l * q.E + beg;
+    // Sum of squares in chunk_sumsq's order, keeping the chunk in shared memory.
+    float a = 0.f;
+    const long long nvec = n / VW;
+    long long v = threadIdx.x;
+    for (; v + 7 * NORM_THREADS < nvec; v += 8 * NORM_THREADS) {
+      uint4 u[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) u[k] = __ldg(reinterpret_cast<const uint4*>(src) + v + k * NORM_THREADS);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        s_chunk[v + k * NORM_THREADS] = u[k];
+        const T* e = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+        for (int i = 0; i < VW; ++i) {
+          const float f = to_f32(e[i]);
+          a = fmaf(f, f, a);
+        }
+      }
+    }
+    for (; v < nvec; v += NORM_THREADS) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + v);
+      s_chunk[v] = u;
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
+        const float f = to_f32(e[i]);
+        a = fmaf(f, f, a);
+      }
+    }
+    for (long long e = nvec * VW + threadIdx.x; e < n; e += NORM_THREADS) {
+      const T xv = src[e];
+      sdata[e] = xv;
+      const float f = to_f32(xv);
+      a = fmaf(f, f, a);
+    }
+    const double tot = block_sum(static_cast<double>(a), s_warp);
+    if (threadIdx.x == 0) {
+      q.partial[l * q.chunks + c] = tot;
+      __threadfence();
+      atomicAdd(q.count + l, 1u);
+      const unsigned need = static_cast<unsigned>(q.chunks);
+      int ok = 1;
+      if (ld_acquire_gpu_u32(q.count + l) < need) {
+        const long long start = clock64();
+        while (ld_acquire_gpu_u32(q.count + l) < need) {
+          __nanosleep(64);
+          if (*reinterpret_cast<volatile int*>(F.status) != 0 || clock64() - start > F.wait_limit) {
+            atomicCAS(F.status, 0, kStatusNormalizeTimeout);
+            ok = 0;
+            break;
+          }
+        }
+      }
+      s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    if (threadIdx.x < 32) {
+      const float den = norm_den(q.partial + l * q.chunks, q.chunks, F.eps);
+      if (threadIdx.x == 0) s_den = den;
+    }
+    __syncthreads();
+    const float den = s_den;
+    __half* out = q.xh + l * q.E + beg;
+    const long long n8 = n / 8;
+    for (long long g = threadIdx.x; g < n8; g += NORM_THREADS) {
+      float f[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = to_f32(sdata[g * 8 + i]);
+      *reinterpret_cast<uint4*>(out + g * 8) = scale8(f, den);
+    }
+    for (long long e = n8 * 8 + threadIdx.x; e < n; e += NORM_THREADS)
+      out[e] = __float2half_rn(__fdiv_rn(to_f32(sdata[e]), den));
+    __syncthreads();  // the next chunk overwrites s_chunk
+  }
+}
+
 // y[l] (R x C, contiguous, type T) = xh[l][:R, :C] (FP16, Rp x Cp).
 template <typename T>
 __global__ void __launch_bounds__(NORM_THREADS)

@@ -19,6 +19,7 @@ enum : int {
   kStatusDrainTimeout = 4,
   kStatusSelftestTimeout = 5,
   kStatusDependencyTimeout = 6,
+  kStatusNormalizeTimeout = 7,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

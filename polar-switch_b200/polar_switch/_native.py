@@ -30,6 +30,7 @@ EXPORTED = (
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
     "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs", "ps_set_chain",
+    "ps_set_fused_normalize",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
     "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
 )
@@ -88,6 +89,7 @@ _SIGNATURES = {
     "ps_launch_count": ([], ctypes.c_longlong),
     "ps_set_cta_pairs": ([_int], _int),
     "ps_set_chain": ([_int], _int),
+    "ps_set_fused_normalize": ([_int], _int),
     "ps_set_max_ctas": ([_int], _int),
     "ps_gns_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "ps_sumsq": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr, _i64, _ptr], _int),
@@ -203,6 +205,15 @@ def set_chain(mode):
     rc = load().ps_set_chain(int(mode))
     if rc < 0:
         check("ps_set_chain", rc)
+    return rc
+
+
+def set_fused_normalize(mode):
+    """Normalisation inside circuits: 1 one read of each contiguous input, 0 (default)
+    two passes. Returns the previous mode."""
+    rc = load().ps_set_fused_normalize(int(mode))
+    if rc < 0:
+        check("ps_set_fused_normalize", rc)
     return rc
 
 

@@ -108,3 +108,11 @@ def test_chain_knob_and_selftest_arguments_without_gpu():
     assert lib.ps_selftest_chain_wait(null, 1 << 20, 1000, null) == _native.PS_ERR_INVALID
     assert lib.ps_selftest_chain_wait(ctypes.c_void_p(256), 1024, 1000, null) == _native.PS_ERR_WORKSPACE
     assert lib.ps_selftest_chain_wait(ctypes.c_void_p(256), 1 << 20, 0, null) == _native.PS_ERR_INVALID
+
+
+def test_fused_normalize_knob_without_gpu():
+    lib = _native.load()
+    assert lib.ps_set_fused_normalize(2) == _native.PS_ERR_INVALID
+    prev = lib.ps_set_fused_normalize(1)
+    assert prev == 0  # default: two passes
+    assert lib.ps_set_fused_normalize(prev) == 1
