@@ -261,6 +261,33 @@ PS_API int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer,
                               int buffers, float eps, void* workspace, int64_t workspace_bytes,
                               void* stream);
 
+/* A Muon update applied in place of storing a problem's result: for every
+ * matrix l of the problem, p[l] <- fl(fl(p[l] * decay) + alpha * fl(u[l])),
+ * u the circuit's result in the problem's y_dtype, rounded to p_dtype where
+ * torch rounds it (training/muon.py:84-86: p.mul_(1 - lr * wd);
+ * p.add_(u.to(p.dtype), alpha=-lr * scale)). p: (L, rows, cols) contiguous
+ * bank of p_dtype (PS_F32, PS_BF16 or PS_F16). p == NULL: store y as usual. */
+typedef struct ps_update {
+  void* p;
+  int p_dtype;
+  float decay, alpha;
+} ps_update;
+
+/* ps_circuit_grouped, with the Muon update of problem i folded into its last
+ * apply when updates[i].p is set: the update never exists in memory, the
+ * parameter bank is read and written once in that kernel's epilogue (y of
+ * that problem is not written and may be NULL). Needs the CTA-pair kernel
+ * (ps_set_cta_pairs(1), the default), an unpadded problem (rows and cols
+ * multiples of 8, contiguous) and a 16-byte aligned bank whose rows are a
+ * multiple of 16 bytes; PS_ERR_UNSUPPORTED otherwise. No single counterpart in
+ * the reference: it replaces orthogonalize-then-update (training/muon.py:
+ * 77-86, train_nanogpt.py's sharded bank update) for banks of stacked
+ * matrices. */
+PS_API int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* updates, int n_probs,
+                                     int n_outer, const float* residuals, const int32_t* n_steps,
+                                     const ps_step* steps, int buffers, float eps, void* workspace,
+                                     int64_t workspace_bytes, void* stream);
+
 /* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 

@@ -316,6 +316,13 @@ ps::pair::PairArgs to_pair(const ps::GemmArgs& g, bool sym) {
   a.b_tri = g.b_tri;
   a.store_mirror = g.store_mirror;
   a.same_ab = g.same_ab;
+  a.upd = g.upd;
+  a.p_dtype = g.p_dtype;
+  a.P = g.P;
+  a.p_ld = g.p_ld;
+  a.p_bs = g.p_bs;
+  a.decay = g.decay;
+  a.upd_alpha = g.upd_alpha;
   a.a_chunk = g.a_chunk;
   a.b_chunk = g.b_chunk;
   a.a2_chunk = g.a2_chunk;
@@ -793,7 +800,14 @@ int apply_launch(bool tall, const CUtensorMap& ta, const CUtensorMap& tb, const 
 
 int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, int64_t cols,
                int64_t x_ld, float residual, int y_dtype, int64_t y_ld, bool tall,
-               cudaStream_t stream, bool tri_b = false) {
+               cudaStream_t stream, bool tri_b = false, const ps_update* upd = nullptr) {
+  if (upd && upd->p) {
+    // Muon update into a parameter bank instead of storing y (CTA-pair path;
+    // the caller has checked the layout): y only needs to be a valid
+    // description of the (L, rows, cols) output for the maps.
+    if (!use_pair(false, tall ? cols : rows))
+      return fail(PS_ERR_UNSUPPORTED, "update-fused apply needs the CTA-pair kernel");
+  }
   if (!b || !x || !y) return fail(PS_ERR_INVALID, "ps_apply: null pointer");
   if (!dims_ok(L, rows, cols) || x_ld < cols || y_ld < cols)
     return fail(PS_ERR_INVALID, "ps_apply: bad sizes");
@@ -829,6 +843,16 @@ int apply_impl(const void* b, const void* x, void* y, int64_t L, int64_t rows, i
     if ((rc = map_mnmajor(&tb, b, n, n, L, n, n * n))) return rc;
   }
   fill_gen_tiles(a, M, N, L);
+  if (upd && upd->p) {
+    a.upd = 1;
+    a.p_dtype = upd->p_dtype == PS_F32 ? ps::kOutF32 : upd->p_dtype == PS_BF16 ? ps::kOutBF16
+                                                                               : ps::kOutF16;
+    a.P = upd->p;
+    a.p_ld = cols;
+    a.p_bs = rows * cols;
+    a.decay = upd->decay;
+    a.upd_alpha = upd->alpha;
+  }
   if (residual != 0.f) {
     a.has_addend = 1;
     a.beta = residual;
@@ -1844,12 +1868,39 @@ int64_t ps_circuit_grouped_workspace_bytes(const ps_problem* probs, int n_probs,
 int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const float* residuals,
                        const int32_t* n_steps, const ps_step* steps, int buffers, float eps,
                        void* workspace, int64_t workspace_bytes, void* stream) {
+  return ps_circuit_grouped_update(probs, nullptr, n_probs, n_outer, residuals, n_steps, steps,
+                                   buffers, eps, workspace, workspace_bytes, stream);
+}
+
+int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* updates, int n_probs,
+                              int n_outer, const float* residuals, const int32_t* n_steps,
+                              const ps_step* steps, int buffers, float eps, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (!workspace) return fail(PS_ERR_INVALID, "ps_circuit: null workspace");
+  if (!probs || n_probs <= 0) return fail(PS_ERR_INVALID, "ps_circuit: bad problem list");
   int rc = validate_table(n_outer, residuals, n_steps, steps, buffers);
   if (rc) return rc;
-  for (int i = 0; i < n_probs; ++i)
-    if (!probs[i].x || !probs[i].y) return fail(PS_ERR_INVALID, "ps_circuit: problem %d has a null pointer", i);
+  for (int i = 0; i < n_probs; ++i) {
+    const bool upd = updates && updates[i].p;
+    if (!probs[i].x || (!probs[i].y && !upd))
+      return fail(PS_ERR_INVALID, "ps_circuit: problem %d has a null pointer", i);
+    if (upd) {
+      const ps_update& u = updates[i];
+      const ps_problem& q = probs[i];
+      if (u.p_dtype != PS_F32 && u.p_dtype != PS_BF16 && u.p_dtype != PS_F16)
+        return fail(PS_ERR_INVALID, "ps_circuit: update %d: parameters must be FP32, BF16 or FP16", i);
+      if (!std::isfinite(u.decay) || !std::isfinite(u.alpha))
+        return fail(PS_ERR_INVALID, "ps_circuit: update %d: factors must be finite", i);
+      if (q.y_dtype != PS_F16 && q.y_dtype != PS_F32 && q.y_dtype != PS_BF16)
+        return fail(PS_ERR_INVALID, "ps_circuit: update %d: y_dtype must be FP16, FP32 or BF16", i);
+      if (q.rows % 8 || q.cols % 8 || !aligned16(u.p) || (q.cols * elem_bytes(u.p_dtype)) % 16 ||
+          !use_pair(false, std::min(q.rows, q.cols)))
+        return fail(PS_ERR_UNSUPPORTED,
+                    "ps_circuit: update %d needs the CTA-pair kernel, rows and cols multiples of 8 "
+                    "and a 16-byte aligned bank with 16-byte rows", i);
+    }
+  }
   DeviceState* st = nullptr;
   if ((rc = device_state(&st))) return rc;
   GroupedPlan plan;
@@ -1888,10 +1939,12 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
   for (int i = 0; i < np; ++i) {
     const ps_problem& q = probs[i];
     const GroupedPlan::Prob& p = plan.probs[i];
-    // The last apply writes straight into y when y's layout allows TMA stores.
-    direct[i] = (q.y_dtype == PS_F16 || q.y_dtype == PS_F32 || q.y_dtype == PS_BF16) &&
-                p.lay.Rp == q.rows && p.lay.Cp == q.cols &&
-                (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 && aligned16(q.y);
+    // The last apply writes straight into y when y's layout allows TMA stores
+    // (or applies the update straight into the bank, checked above).
+    direct[i] = (updates && updates[i].p) ||
+                ((q.y_dtype == PS_F16 || q.y_dtype == PS_F32 || q.y_dtype == PS_BF16) &&
+                 p.lay.Rp == q.rows && p.lay.Cp == q.cols &&
+                 (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 && aligned16(q.y));
   }
   // Chain launches count completed tiles per matrix from zero within this call.
   int off = 0;
@@ -1944,8 +1997,10 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
       const ps_problem& q = probs[i];
       const int64_t Rp = p.lay.Rp, Cp = p.lay.Cp;
       if (final_iter && direct[i]) {
-        rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], q.y, q.L, Rp, Cp, Cp,
-                        residuals[t], q.y_dtype, q.cols, p.lay.tall, s, tri);
+        const bool upd = updates && updates[i].p;
+        rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], upd ? updates[i].p : q.y, q.L, Rp,
+                        Cp, Cp, residuals[t], q.y_dtype, q.cols, p.lay.tall, s, tri,
+                        upd ? &updates[i] : nullptr);
       } else {
         rc = apply_impl(buf_ptr(i, last), ws + p.xh_off[cur[i]], ws + p.xh_off[1 - cur[i]], q.L,
                         Rp, Cp, Cp, residuals[t], PS_F16, Cp, p.lay.tall, s, tri);

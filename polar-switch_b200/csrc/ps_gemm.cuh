@@ -77,6 +77,12 @@ struct GemmArgs {
   // CTA-pair path only: the operand map is a 4-D chunked map (one TMA per
   // 128-wide K stage, see ps_gemm2.cuh); the one-CTA kernel ignores these.
   int a_chunk, b_chunk, a2_chunk, b2_chunk;
+  // CTA-pair path only: Muon update of a parameter bank in place of the
+  // output store (see pair::PairArgs).
+  int upd, p_dtype;
+  void* P;
+  long long p_ld, p_bs;
+  float decay, upd_alpha;
   int* status;               // device status word
   long long wait_limit;      // cycles before a bounded wait gives up
 };

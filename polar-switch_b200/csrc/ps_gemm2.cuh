@@ -38,6 +38,8 @@
 // half the operand bytes from L2.
 #pragma once
 
+#include <type_traits>
+
 #include "ps_gemm.cuh"
 
 namespace ps {
@@ -135,9 +137,68 @@ struct PairArgs {
   int store_mirror;       // symmetric: also store the transposed off-diagonal blocks
   int same_ab;            // symmetric A . A^T, A and B maps identical (see below)
   int a_chunk, b_chunk, a2_chunk, b2_chunk;  // map is 4-D chunked (one TMA per stage)
+  // General products only: instead of storing the result, apply it as a
+  // Muon update to a parameter bank P (same layout as the output):
+  // p <- fl(fl(p * decay) + upd_alpha * fl(u)), u the result in the output type.
+  int upd, p_dtype;
+  void* P;
+  long long p_ld, p_bs;
+  float decay, upd_alpha;
   int* status;
   long long wait_limit;
 };
+
+// The Muon update of one output row's 32 values (the FP32 epilogue values f,
+// before the circuit's FP16 rounding) into row `row` of parameter matrix b of
+// type T: u = OUT(fp16(f)) as the circuit would store it, then p <- fl_T(fma(
+// alpha, fl_T(u), fl_T(p * decay))) as ps_muon_update_kernel computes it.
+template <int OUT, typename T>
+__device__ __forceinline__ void update_row_t(const PairArgs& a, int b, int row, int col0, int nv,
+                                             const float (&f)[32]) {
+  T* p = static_cast<T*>(a.P) + static_cast<long long>(b) * a.p_bs +
+         static_cast<long long>(row) * a.p_ld + col0;
+  auto rnd = [](float v) -> float {
+    if (std::is_same<T, float>::value) return v;
+    if (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(v));
+    return __half2float(__float2half_rn(v));
+  };
+  auto to_f = [](T v) -> float {
+    if constexpr (std::is_same<T, float>::value) return v;
+    else if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(v);
+    else return __half2float(v);
+  };
+  auto from_f = [](float v) -> T {
+    if constexpr (std::is_same<T, float>::value) return v;
+    else if constexpr (std::is_same<T, __nv_bfloat16>::value) return __float2bfloat16_rn(v);
+    else return __float2half_rn(v);
+  };
+  constexpr int VW = 16 / sizeof(T);
+  if (nv >= 32) {
+#pragma unroll
+    for (int v = 0; v < 32 / VW; ++v) {
+      uint4 raw = ld_global_v4(p + v * VW);
+      T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
+        const int j = v * VW + i;
+        float u = __half2float(__float2half_rn(f[j]));
+        if (OUT == kOutBF16) u = __bfloat162float(__float2bfloat16_rn(u));
+        const float w1 = rnd(__fmul_rn(to_f(e[i]), a.decay));
+        e[i] = from_f(__fmaf_rn(a.upd_alpha, rnd(u), w1));
+      }
+      st_global_v4(p + v * VW, raw);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j >= nv) break;
+      float u = __half2float(__float2half_rn(f[j]));
+      if (OUT == kOutBF16) u = __bfloat162float(__float2bfloat16_rn(u));
+      const float w1 = rnd(__fmul_rn(to_f(p[j]), a.decay));
+      p[j] = from_f(__fmaf_rn(a.upd_alpha, rnd(u), w1));
+    }
+  }
+}
 
 template <bool SYM>
 __device__ __forceinline__ void decode(const PairArgs& a, int t, uint32_t rank, int& b, int& m0,
@@ -422,6 +483,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (j == d) f[j] += args.diag;
+        }
+        if (!SYM && args.upd) {
+          if (grow < args.M) {
+            const int nv = ncols_total - gcol0;
+            if (args.p_dtype == kOutF32)
+              update_row_t<OUT, float>(args, b, grow, gcol0, nv, f);
+            else if (args.p_dtype == kOutBF16)
+              update_row_t<OUT, __nv_bfloat16>(args, b, grow, gcol0, nv, f);
+            else
+              update_row_t<OUT, __half>(args, b, grow, gcol0, nv, f);
+          }
+          return;
         }
         uint32_t w[32];
         convert_row<OUT>(f, w);

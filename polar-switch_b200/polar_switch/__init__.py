@@ -132,13 +132,20 @@ class _Circuit:
         return out
 
 
-    def grouped(self, banks, epsilon, outs=None):
+    def grouped(self, banks, epsilon, outs=None, updates=None):
         """Run the circuit on several tensors of different shapes in one C call.
 
         Tensors that share n = min(rows, cols) have their inner iterations
         batched into one launch each. Returns one output per input (its dtype
         and shape unless ``outs`` supplies tensors, which may be FP16 to
         receive the circuit's FP16 result without widening).
+
+        ``updates``: optional list with, per input, None or a tuple
+        ``(param_bank, decay, alpha)``: the result u of that input is not
+        returned but applied as ``p <- p * decay + alpha * u`` (Muon's update,
+        rounded as torch's ``p.mul_(decay); p.add_(u.to(p.dtype), alpha)``) to
+        the contiguous bank of the input's shape, inside the last apply
+        (ps_circuit_grouped_update). Its entry in the returned list is None.
         """
         if not banks:
             return []
@@ -146,29 +153,48 @@ class _Circuit:
         device = banks[0].device
         works, results = [], []
         probs = (nat.PsProblem * len(banks))()
+        upd = None
+        if updates is not None:
+            upd = (nat.PsUpdate * len(banks))()
         for i, X in enumerate(banks):
             if X.device != device:
                 raise ValueError("all tensors of a grouped call must be on one device")
             if X.dtype not in nat.DTYPE_CODES:
                 raise TypeError(f"Unsupported dtype {X.dtype}")
             W = X.reshape(-1, *X.shape[-2:])
-            Y = outs[i] if outs is not None else torch.empty(X.shape, device=device, dtype=X.dtype)
-            if Y.shape != X.shape or not Y.is_contiguous() or Y.dtype not in nat.DTYPE_CODES:
-                raise ValueError("each output must be contiguous with its input's shape")
+            target = updates[i] if updates is not None else None
+            if target is not None:
+                P, decay, alpha = target
+                if (P.shape != X.shape or not P.is_contiguous() or P.device != device
+                        or P.dtype not in (torch.float32, torch.bfloat16, torch.float16)):
+                    raise ValueError("an update target must be a contiguous FP32/BF16/FP16 bank of "
+                                     "its input's shape on the same device")
+                upd[i] = nat.PsUpdate(P.data_ptr(), nat.DTYPE_CODES[P.dtype], float(decay), float(alpha))
+                Y = None
+            else:
+                Y = outs[i] if outs is not None else torch.empty(X.shape, device=device, dtype=X.dtype)
+                if Y.shape != X.shape or not Y.is_contiguous() or Y.dtype not in nat.DTYPE_CODES:
+                    raise ValueError("each output must be contiguous with its input's shape")
             works.append(W)
             results.append(Y)
             L, rows, cols = W.shape
             sL, sR, sC = W.stride()
             probs[i] = nat.PsProblem(W.data_ptr(), nat.DTYPE_CODES[X.dtype], L, rows, cols, sL, sR, sC,
-                                     Y.data_ptr(), nat.DTYPE_CODES[Y.dtype])
+                                     Y.data_ptr() if Y is not None else None,
+                                     nat.DTYPE_CODES[Y.dtype if Y is not None else X.dtype])
         with torch.cuda.device(device):
             ws_bytes = lib.ps_circuit_grouped_workspace_bytes(probs, len(banks), self.buffers)
             if ws_bytes < 0:
                 nat.check("ps_circuit_grouped_workspace_bytes", nat.PS_ERR_INVALID)
             ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8)
-            nat.check("ps_circuit_grouped", lib.ps_circuit_grouped(
-                probs, len(banks), self.n_outer, self.residuals, self.n_steps, self.steps,
-                self.buffers, float(epsilon), nat.ptr(ws), ws_bytes, nat.stream_ptr(device)))
+            if upd is None:
+                nat.check("ps_circuit_grouped", lib.ps_circuit_grouped(
+                    probs, len(banks), self.n_outer, self.residuals, self.n_steps, self.steps,
+                    self.buffers, float(epsilon), nat.ptr(ws), ws_bytes, nat.stream_ptr(device)))
+            else:
+                nat.check("ps_circuit_grouped_update", lib.ps_circuit_grouped_update(
+                    probs, upd, len(banks), self.n_outer, self.residuals, self.n_steps, self.steps,
+                    self.buffers, float(epsilon), nat.ptr(ws), ws_bytes, nat.stream_ptr(device)))
         return results
 
 
@@ -231,11 +257,13 @@ def make_polynomial_orthogonalizer(method, compile=True, epsilon=1e-7):
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
 
-    def grouped(tensors, outs=None):
-        """Orthogonalize a list of tensors of different shapes in one grouped call."""
+    def grouped(tensors, outs=None, updates=None):
+        """Orthogonalize a list of tensors of different shapes in one grouped call
+        (``updates``: fold Muon's update of a parameter bank into the last apply,
+        see _Circuit.grouped)."""
         for X in tensors:
             _check_input(X)
-        result = circuit.grouped(list(tensors), epsilon, outs=outs)
+        result = circuit.grouped(list(tensors), epsilon, outs=outs, updates=updates)
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
 

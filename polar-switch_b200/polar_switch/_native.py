@@ -30,7 +30,7 @@ EXPORTED = (
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
     "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs", "ps_set_chain",
-    "ps_set_fused_normalize",
+    "ps_set_fused_normalize", "ps_circuit_grouped_update",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
     "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
 )
@@ -50,6 +50,13 @@ class PsProblem(ctypes.Structure):
                 ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("sL", ctypes.c_int64),
                 ("sR", ctypes.c_int64), ("sC", ctypes.c_int64), ("y", ctypes.c_void_p),
                 ("y_dtype", ctypes.c_int32)]
+
+
+class PsUpdate(ctypes.Structure):
+    """Mirror of `ps_update`: a Muon update folded into a problem's last apply."""
+
+    _fields_ = [("p", ctypes.c_void_p), ("p_dtype", ctypes.c_int32), ("decay", ctypes.c_float),
+                ("alpha", ctypes.c_float)]
 
 
 class NativeError(RuntimeError):
@@ -109,6 +116,9 @@ _SIGNATURES = {
     "ps_circuit_grouped": ([ctypes.POINTER(PsProblem), _int, _int, ctypes.POINTER(_f32),
                             ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep), _int, _f32,
                             _ptr, _i64, _ptr], _int),
+    "ps_circuit_grouped_update": ([ctypes.POINTER(PsProblem), ctypes.POINTER(PsUpdate), _int, _int,
+                                   ctypes.POINTER(_f32), ctypes.POINTER(ctypes.c_int32),
+                                   ctypes.POINTER(PsStep), _int, _f32, _ptr, _i64, _ptr], _int),
 }
 
 

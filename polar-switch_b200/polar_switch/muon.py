@@ -198,9 +198,10 @@ class ShardedMuon(torch.optim.Optimizer):
          the "rms" scale);
       3. the local chunks of all banks are orthogonalized in one grouped call;
       4. the local slice of every bank gets the decoupled weight decay and the
-         scaled update (ps_muon_update), and all_gather_into_tensor writes every
-         rank's slice into every rank's bank, each gather issued as soon as its
-         slice is updated.
+         scaled update -- by default inside the last apply of its circuit
+         (ps_circuit_grouped_update: the update never exists in memory), else
+         with ps_muon_update -- and all_gather_into_tensor writes every rank's
+         slice into every rank's bank.
 
     With a `norm_log` (polar_switch.diagnostics.NormLog) every local chunk's
     orthogonalized update is recorded before it is applied, labelled with the
@@ -218,12 +219,13 @@ class ShardedMuon(torch.optim.Optimizer):
     """
 
     def __init__(self, banks, orthogonalize, lr, momentum=0.95, weight_decay=0.0, scale="rms",
-                 group=None, norm_log=None):
+                 group=None, norm_log=None, fuse_update=True):
         banks = list(banks)
         super().__init__(banks, dict(lr=lr, momentum=momentum, weight_decay=weight_decay, scale=scale))
         self.orthogonalize = orthogonalize
         self.group = group
         self.norm_log = norm_log
+        self.fuse_update = fuse_update
         if torch.distributed.is_available() and torch.distributed.is_initialized():
             self.world_size = torch.distributed.get_world_size(group)
             self.rank = torch.distributed.get_rank(group)
@@ -240,6 +242,18 @@ class ShardedMuon(torch.optim.Optimizer):
 
     def _update(self, param_chunk, update, decay, alpha):
         muon_update(list(param_chunk.unbind(0)), update, decay, alpha)
+
+    def _fusable(self, grouped, entries):
+        """Whether the update can be folded into the orthogonalization: this
+        package's grouped orthogonalizer, no update log (it needs the update
+        tensor), the library's own update step, and banks the update-fused
+        circuit takes (CUDA, FP32/BF16/FP16, rows and columns multiples of 8;
+        the CTA-pair kernel, the default, is checked by the library)."""
+        if (not self.fuse_update or grouped is None or self.norm_log is not None
+                or type(self)._update is not ShardedMuon._update):
+            return False
+        return all(bank.is_cuda and bank.dtype in (torch.float32, torch.bfloat16, torch.float16)
+                   and bank.shape[-1] % 8 == 0 and bank.shape[-2] % 8 == 0 for _, bank, _, _ in entries)
 
     @torch.no_grad()
     def step(self):
@@ -272,6 +286,22 @@ class ShardedMuon(torch.optim.Optimizer):
             out_dtype = torch.bfloat16 if g["scale"] == "rms" else bank.dtype
             directions.append(self._directions(local, state["momentum_chunk"], g["momentum"], out_dtype))
         grouped = getattr(self.orthogonalize, "grouped", None)
+        if self._fusable(grouped, entries):
+            # Step 4 folded into the circuits' last applies: each local slice
+            # receives its update inside the kernel that computes it.
+            targets = []
+            for g, bank, _, _ in entries:
+                rows, cols = bank.shape[-2:]
+                factor = (0.2 * math.sqrt(max(rows, cols)) if g["scale"] == "rms"
+                          else math.sqrt(rows / cols))
+                targets.append((self._chunk(bank)[1], 1 - g["lr"] * g["weight_decay"], -g["lr"] * factor))
+            grouped(directions, updates=targets)
+            if W > 1:
+                works = [dist.all_gather_into_tensor(bank.data, self._chunk(bank)[1], group=self.group,
+                                                     async_op=True) for _, bank, _, _ in entries]
+                for work in works:
+                    work.wait()
+            return
         updates = grouped(directions) if grouped is not None else [self.orthogonalize(d) for d in directions]
         gathers = []
         for i, ((g, bank, _, _), update) in enumerate(zip(entries, updates)):

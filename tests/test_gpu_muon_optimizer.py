@@ -163,3 +163,44 @@ def test_fp32_gradients_on_bf16_weights(cuda_device):
     for p, r, m in zip(params, ref_params, ref_moms):
         assert torch.equal(opt.state[p]["momentum_buffer"], m)
         assert float((p.detach().float() - r.float()).norm() / r.float().norm()) < 1e-3
+
+
+@pytest.mark.parametrize("pdtype", [torch.float32, torch.bfloat16])
+def test_update_folded_into_the_last_apply_equals_the_update_kernel(cuda_device, pdtype):
+    """grouped(..., updates=...) applies p <- p * decay + alpha * u inside the
+    circuit's last apply; it must give the bits of the circuit's output followed
+    by ps_muon_update (itself tested against torch's sequence above)."""
+    from polar_switch.muon import muon_update
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    shapes = [(3, 256, 512), (2, 384, 128), (4, 192, 192)]
+    dirs = [seeded(s, 800 + i).to(cuda_device).bfloat16() for i, s in enumerate(shapes)]
+    banks = [(seeded(s, 810 + i) * 0.02).to(cuda_device, pdtype) for i, s in enumerate(shapes)]
+    ref = [b.clone() for b in banks]
+    factors = [(1 - 0.02 * 0.1, -0.02 * (0.2 * max(s[1:]) ** 0.5)) for s in shapes]
+    outs = polar.grouped(dirs)
+    for r, u, (decay, alpha) in zip(ref, outs, factors):
+        muon_update(list(r.unbind(0)), u.contiguous(), decay, alpha)
+    got = polar.grouped(dirs, updates=[(b, d, a) for b, (d, a) in zip(banks, factors)])
+    assert all(o is None for o in got)
+    for b, r in zip(banks, ref):
+        assert torch.equal(b, r)
+
+
+def test_sharded_muon_fused_update_equals_unfused(cuda_device):
+    from polar_switch.muon import ShardedMuon
+    shapes = [(3, 256, 128), (4, 128, 384), (2, 192, 192)]
+    base = [seeded(s, 820 + i).to(cuda_device) * 0.05 for i, s in enumerate(shapes)]
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    fused = [torch.nn.Parameter(b.clone()) for b in base]
+    plain = [torch.nn.Parameter(b.clone()) for b in base]
+    opt_f = ShardedMuon(fused, polar, lr=0.02, weight_decay=0.1, fuse_update=True)
+    opt_p = ShardedMuon(plain, polar, lr=0.02, weight_decay=0.1, fuse_update=False)
+    for step in range(2):
+        grads = [seeded(s, 830 + 10 * step + i).to(cuda_device) for i, s in enumerate(shapes)]
+        for p, q, gr in zip(fused, plain, grads):
+            p.grad = gr.clone()
+            q.grad = gr.clone()
+        opt_f.step()
+        opt_p.step()
+    for a, b in zip(fused, plain):
+        assert torch.equal(a.detach(), b.detach())

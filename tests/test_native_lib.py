@@ -63,6 +63,8 @@ def test_struct_layouts_match_header():
     # ps_step: 3 x int32 + 3 x float; ps_problem: pointers and int64 fields
     assert ctypes.sizeof(_native.PsStep) == 24
     assert ctypes.sizeof(_native.PsProblem) == 8 + 8 + 6 * 8 + 8 + 8
+    # ps_update: pointer, int32 dtype, two floats (padded to 8-byte alignment)
+    assert ctypes.sizeof(_native.PsUpdate) == 24
 
 
 def test_host_side_knobs_round_trip_without_gpu():
