@@ -84,26 +84,40 @@ def test_grouped_matches_single_calls(cuda_device):
 
 def test_grouped_many_buckets_batched_launches(cuda_device):
     """More buckets than one launch takes (8 problems per launch): every
-    bucket still equals its own call bit for bit, and the Grams and applies
-    of all buckets run in a few batched launches per outer iteration."""
+    bucket still equals its own call bit for bit. On the one-CTA kernel the
+    Grams and applies of all buckets run in a few batched launches per outer
+    iteration; on CTA pairs (the default) in one launch per bucket."""
     from polar_switch import _native as nat
     from polar_switch import make_polynomial_orthogonalizer
     polar = make_polynomial_orthogonalizer("PS2_55")
     shapes = [(2, 256, 128), (1, 128, 256), (2, 136, 136), (1, 384, 128), (3, 128, 128),
               (1, 128, 512), (2, 264, 128), (1, 128, 200), (2, 520, 128), (1, 128, 640)]
     banks = [seeded(s, 47 + i).to(cuda_device) for i, s in enumerate(shapes)]
-    nat.profile_enable(True)
-    grouped = polar.grouped(banks)
-    prof = nat.profile_read()
-    nat.profile_enable(False)
+    prev = nat.set_cta_pairs(0)
+    try:
+        nat.profile_enable(True)
+        grouped = polar.grouped(banks)
+        prof = nat.profile_read()
+        nat.profile_enable(False)
+        singles = [polar(b) for b in banks]
+    finally:
+        nat.set_cta_pairs(prev)
     # 2 outer iterations; per iteration Grams: tall and wide variants (5 problems each),
     # applies: one variant for all 10 problems -> 2 launches of 8 + 2
     assert prof["gram"]["launches"] == 2 * 2
     assert prof["apply"]["launches"] == 2 * 2
+    nat.profile_enable(True)
+    grouped_pairs = polar.grouped(banks)
+    prof_pairs = nat.profile_read()
+    nat.profile_enable(False)
+    assert prof_pairs["gram"]["launches"] == 2 * len(shapes)
+    assert prof_pairs["apply"]["launches"] == 2 * len(shapes)
+    for b, g in zip(banks, grouped_pairs):
+        assert torch.equal(g, polar(b))
     # the normalisations: 8 + 2 problems of one input type, two passes each
     assert prof["normalize"]["launches"] == 2 * 2
-    for b, g in zip(banks, grouped):
-        assert torch.equal(g, polar(b))
+    for g, single in zip(grouped, singles):
+        assert torch.equal(g, single)
 
 
 def test_grouped_normalisations_batched_by_type(cuda_device):
