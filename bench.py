@@ -122,7 +122,8 @@ def roofline_entry(name, v, steps, n_dom, clocks, peaks, traffic_table):
            "frac": (traffic or alg_bytes) / sec / 1e9 / hbm}
     bound = "hbm" if ai < ridge else "tensor"
     main = mem if bound == "hbm" else tensor
-    return {"bound": bound, "kernel": f"ps_gemm ({name})", "achieved": main["achieved"],
+    label = "ps_circuit_pair_kernel (whole circuits)" if name == "circuit" else f"ps_gemm ({name})"
+    return {"bound": bound, "kernel": label, "achieved": main["achieved"],
             "peak": main["peak"], "unit": "GB/s" if bound == "hbm" else "TFLOP/s", "frac": main["frac"],
             "peak_source": f"{src}: {'HBM copy' if bound == 'hbm' else 'bf16 ' + tname}",
             "traffic": traffic, "traffic_source": traffic_src,
@@ -414,6 +415,30 @@ def time_single_8192(device, warmup, calls=15):
             "published_ms": 7.47, "vs_published": 7.47 / ms, "clocks": clocks.summary()}
 
 
+# Upper end of each method's published singular-value interval for inputs
+# with sigma in [1e-3, 1] (reference README.md:64-73; GNS polar_switch/README.md).
+DESIGN_TOP = {"PS2_55": 1.106236, "PS3_55": 1.080954, "GNS": 1.212979}
+
+
+def sweep_output_check(Y, method, iters=30):
+    """Cheap sanity check of a sweep output: finite, largest singular value (by
+    power iteration on Y^T Y in FP32, per matrix) at most the method's design
+    top plus 1e-2, and mean squared singular value in [0.5, 1.3]. A skipped or
+    duplicated tile breaks at least one of these."""
+    Yf = Y.float()
+    finite = bool(torch.isfinite(Yf).all())
+    n = min(Yf.shape[-2:])
+    gen = torch.Generator(device=Y.device).manual_seed(5)
+    v = torch.randn(Yf.shape[0], Yf.shape[-1], 1, device=Y.device, generator=gen)
+    for _ in range(iters):
+        v = Yf.mT @ (Yf @ v)
+        v = v / v.norm(dim=(-2, -1), keepdim=True)
+    smax = float((Yf @ v).norm(dim=(-2, -1)).max())
+    fro2 = float((Yf.pow(2).sum(dim=(-2, -1)) / n).mean())
+    ok = finite and smax <= DESIGN_TOP.get(method, 1.25) + 1e-2 and 0.5 <= fro2 <= 1.3
+    return {"finite": finite, "sigma_max_est": round(smax, 5), "mean_sigma2": round(fro2, 4), "ok": ok}
+
+
 def run_sweep(args):
     """--sweep: median latency of whole circuits on the shapes whose reference
     latency is published, one JSON line per (shape, method). Inputs are FP16
@@ -458,7 +483,9 @@ def run_sweep(args):
                     times.append(s.elapsed_time(e))
             times.sort()
             ms = times[len(times) // 2]
+            check = sweep_output_check(polar(X), method)
             print(json.dumps({"shape": list(shape), "method": method, "median_ms": round(ms, 4),
+                              "output_check": check,
                               "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
                               "frac_of_measured_burst_peak": round(flops / (ms * 1e-3) / 1e12 / peak, 3),
                               "published_ms": pub[method],
@@ -617,7 +644,8 @@ def main():
     if rank == 0:
         peaks = load_peaks()
         clock_summary = clocks.summary()
-        gemm_kinds = {k: v for k, v in prof.items() if k in ("gram", "square", "apply") and v["launches"]}
+        gemm_kinds = {k: v for k, v in prof.items()
+                      if k in ("gram", "square", "apply", "circuit") and v["launches"]}
         dom_name, dom = max(gemm_kinds.items(), key=lambda kv: kv[1]["ms"])
         n_dom = min(min(r, c) for _, r, c in shapes)
         roofline = roofline_entry(dom_name, dom, args.steps, n_dom, clock_summary, peaks, load_traffic_table())

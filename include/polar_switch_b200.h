@@ -111,7 +111,8 @@ PS_API long long ps_launch_count(void);
 /* Profiling of the library's own launches: enable=1 clears the records and
  * brackets every later launch with CUDA events on its stream; enable=0 stops
  * recording. ps_profile_read waits for the recorded launches of one class
- * (0 normalise, 1 gram, 2 square/symmetric product, 3 apply, 4 other) and
+ * (0 normalise, 1 gram, 2 square/symmetric product, 3 apply, 4 other,
+ * 5 whole circuit in one launch) and
  * returns their summed device time, count, algorithmic FLOPs and algorithmic
  * HBM bytes. */
 PS_API int ps_profile_enable(int enable);
@@ -135,6 +136,15 @@ PS_API int ps_set_cta_pairs(int mode);
  * in the reference (its inner loop, polar_switch/__init__.py:42-43, issues one
  * kernel per inner iteration). */
 PS_API int ps_set_chain(int mode);
+
+/* How ps_circuit / ps_circuit_grouped run on the CTA-pair path: 1 = one
+ * persistent launch for every stage of every problem (each matrix's Gram,
+ * inner iterations and apply chained through per-matrix completion counters,
+ * bounded waits), 0 (default) = one launch per stage. Same bits either way;
+ * up to 8 problems, 3 buffers and 48 stages (else per-stage launches).
+ * Returns the previous mode (PS_ERR_INVALID for other values). Replaces the
+ * whole loop of polar_switch/__init__.py:40-44 with one launch. */
+PS_API int ps_set_circuit_kernel(int mode);
 
 /* How ps_circuit / ps_circuit_grouped normalise contiguous, unpadded inputs:
  * 1 = one read of the input (a persistent kernel keeps each chunk in shared

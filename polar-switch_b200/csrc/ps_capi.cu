@@ -21,6 +21,7 @@
 #include "ps_gemm.cuh"
 #include "ps_gemm2.cuh"
 #include "ps_chain.cuh"
+#include "ps_circuit.cuh"
 #include "ps_norm.cuh"
 #include "ps_muon.cuh"
 #include "ps_stats.cuh"
@@ -49,7 +50,8 @@ enum ProfKind : int {
   kProfSquare = 2,
   kProfApply = 3,
   kProfOther = 4,
-  kNumProfKinds = 5
+  kProfCircuit = 5,  // whole circuits in one launch (ps_circuit.cuh)
+  kNumProfKinds = 6
 };
 
 thread_local std::string g_last_error;
@@ -68,6 +70,9 @@ int g_max_ctas = 0;
 // persistent chain launch per outer iteration (1, default) or one launch per
 // inner iteration (0). Both give the same bits.
 int g_chain_mode = 1;
+// A grouped circuit on the CTA-pair path runs as one persistent launch for all
+// its stages (1) or one launch per stage (0). Same bits either way.
+int g_circuit_mode = 0;
 // Normalisations of grouped circuits read each contiguous input once (the
 // fused single-read kernel) when 1, or run the two passes when 0 (default).
 // Both give the same bits; the single read measured slower on the Qwen step
@@ -150,6 +155,8 @@ struct DeviceState {
   int pair_clusters[kNumVariants] = {};
   bool chain_ready = false;
   int chain_clusters = 0;
+  bool circ_ready = false;
+  int circ_clusters = 0;
   int norm_fused_grid[4] = {};  // resident CTAs of the fused normalisation, by dtype
 };
 
@@ -1330,6 +1337,7 @@ struct GroupedPlan {
   std::vector<Prob> probs;
   std::vector<NGroup> groups;
   int64_t ctr_off = 0, ctr_bytes = 0;  // all groups' counters, one contiguous range
+  int64_t circ_off = 0;                 // whole-circuit kernel counters (inside that range)
   int64_t total = 0;
 };
 
@@ -1377,8 +1385,218 @@ int make_grouped_plan(const ps_problem* probs, int n_probs, int buffers, int sms
     plan->probs[i].cnt_off = off;
     off += round_up(probs[i].L * static_cast<int64_t>(sizeof(unsigned)), 256);
   }
+  int64_t ltot = 0;
+  for (int i = 0; i < n_probs; ++i) ltot += probs[i].L;
+  plan->circ_off = off;  // whole-circuit kernel: one counter per matrix of every problem
+  off += round_up(ltot * static_cast<int64_t>(sizeof(unsigned)), 256);
   plan->ctr_bytes = off - plan->ctr_off;
   plan->total = off;
+  return PS_OK;
+}
+
+// ------------------------------------------------------------------ whole circuit
+// Whether a grouped circuit runs as one ps_circuit_pair_kernel launch: the
+// CTA-pair path for every problem and the kernel's table limits.
+bool use_circuit_kernel(const GroupedPlan& plan, int n_probs, int n_outer, const int32_t* n_steps,
+                        int buffers) {
+  if (!g_circuit_mode || n_probs > ps::circ::MAXP || buffers > ps::circ::MAXB) return false;
+  int stages = 0, steps = 0;
+  for (int t = 0; t < n_outer; ++t) {
+    stages += n_steps[t] + 2;
+    steps += n_steps[t];
+  }
+  if (stages > ps::circ::MAX_STAGES || steps > ps::circ::MAX_STEPS) return false;
+  for (const GroupedPlan::Prob& p : plan.probs)
+    if (!use_pair(true, p.lay.n) || !use_pair(false, p.lay.n)) return false;
+  return true;
+}
+
+// All stages of a grouped circuit in one launch (ps_circuit.cuh). `cur0` is
+// the Xh buffer holding the normalised inputs; the final applies store into
+// y (direct problems) or Xh[1 - final cur] (the caller copies those out).
+int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const ps_update* updates,
+                       int n_probs, int n_outer, const float* residuals, const int32_t* n_steps,
+                       const ps_step* steps, int buffers, uint8_t* ws, const std::vector<bool>& direct,
+                       cudaStream_t stream) {
+  using ps::circ::CircuitParams;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  auto kern = ps::circ::ps_circuit_pair_kernel;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(ps::pair::NUM_THREADS);
+  cfg.dynamicSmemBytes = ps::pair::SMEM_TOTAL;
+  cfg.stream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  if (!st->circ_ready) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         ps::pair::SMEM_TOTAL);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(circuit smem)");
+    cfg.gridDim = dim3(2 * (st->sms / 2));
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters(circuit)");
+    if (clusters < 1) return fail(PS_ERR_UNSUPPORTED, "no co-resident CTA pair fits on the device");
+    st->circ_clusters = clusters;
+    st->circ_ready = true;
+  }
+  static thread_local CircuitParams P;
+  std::memset(&P, 0, sizeof(P));
+  // stage table
+  int ns = 0, off = 0, nsym = 0, napp = 0;
+  for (int t = 0; t < n_outer; ++t) {
+    auto add_stage = [&](int kind, int step) {
+      P.st_kind[ns] = static_cast<unsigned char>(kind);
+      P.st_t[ns] = static_cast<unsigned char>(t);
+      P.st_step[ns] = static_cast<unsigned char>(step);
+      P.st_nsym[ns] = static_cast<unsigned char>(nsym);
+      P.st_napp[ns] = static_cast<unsigned char>(napp);
+      ++ns;
+      if (kind == ps::circ::kApply)
+        ++napp;
+      else
+        ++nsym;
+    };
+    add_stage(ps::circ::kGram, 0);
+    for (int k = 0; k < n_steps[t]; ++k) add_stage(ps::circ::kSquare, off + k);
+    add_stage(ps::circ::kApply, off + n_steps[t] - 1);
+    P.residual[t] = residuals[t];
+    off += n_steps[t];
+  }
+  for (int i = 0; i < off; ++i)
+    P.steps[i] = {steps[i].dst, steps[i].src, steps[i].add, steps[i].alpha, steps[i].beta,
+                  steps[i].diag};
+  P.n_outer = n_outer;
+  P.n_stages = ns;
+  P.nprob = n_probs;
+  int pairs = st->circ_clusters;
+  if (g_max_ctas > 1 && pairs > g_max_ctas / 2) pairs = g_max_ctas / 2;
+  // per problem: maps, shapes, tiles, chunking
+  std::vector<int64_t> total_per_mat(n_probs);
+  int64_t g0 = 0;
+  for (int i = 0; i < n_probs; ++i) {
+    const GroupedPlan::Prob& p = plan.probs[i];
+    const GroupedPlan::NGroup& g = plan.groups[p.group];
+    const ps_problem& q = probs[i];
+    ps::circ::CProblem& c = P.prob[i];
+    const int64_t Rp = p.lay.Rp, Cp = p.lay.Cp, n = p.lay.n, L = q.L;
+    int ck = 0, ck2 = 0;
+    for (int x = 0; x < 2; ++x) {
+      uint8_t* xh = ws + p.xh_off[x];
+      if ((rc = map_pair_operand(&c.xk[x], xh, false, Cp, Rp, L, Cp, Rp * Cp, &ck))) return rc;
+      if ((rc = map_pair_operand(&c.xm[x], xh, true, Cp, Rp, L, Cp, Rp * Cp, &ck2))) return rc;
+      if ((rc = map_out(&c.xo[x], xh, PS_F16, Cp, Rp, L, Cp, Rp * Cp))) return rc;
+      c.xh[x] = reinterpret_cast<const __half*>(xh);
+    }
+    if (ck != ck2) return fail(PS_ERR_INVALID, "internal: X maps disagree on the chunked layout");
+    c.ck_x = ck;
+    for (int k = 0; k < buffers; ++k) {
+      uint8_t* bp = ws + g.buf_off + k * g.buf_bytes + p.goff * n * n * 2;
+      if ((rc = map_pair_operand(&c.bk[k], bp, false, n, n, L, n, n * n, &ck))) return rc;
+      if ((rc = map_pair_operand(&c.bm[k], bp, true, n, n, L, n, n * n, &ck2))) return rc;
+      if ((rc = map_out(&c.bo[k], bp, PS_F16, n, n, L, n, n * n))) return rc;
+      c.buf[k] = reinterpret_cast<const __half*>(bp);
+    }
+    if (ck != ck2) return fail(PS_ERR_INVALID, "internal: buffer maps disagree on the chunked layout");
+    c.ck_b = ck;
+    const bool upd = updates && updates[i].p;
+    c.direct = direct[i] ? 1 : 0;
+    c.y_out = q.y_dtype == PS_F32 ? ps::kOutF32 : q.y_dtype == PS_BF16 ? ps::kOutBF16 : ps::kOutF16;
+    if (direct[i] && !upd) {
+      if ((rc = map_out(&c.yo, q.y, q.y_dtype, q.cols, q.rows, L, q.cols, q.rows * q.cols))) return rc;
+    }
+    if (upd) {
+      c.upd = 1;
+      c.p_dtype = updates[i].p_dtype == PS_F32 ? ps::kOutF32
+                  : updates[i].p_dtype == PS_BF16 ? ps::kOutBF16 : ps::kOutF16;
+      c.P = updates[i].p;
+      c.decay = updates[i].decay;
+      c.upd_alpha = updates[i].alpha;
+    }
+    c.L = static_cast<int>(L);
+    c.Rp = static_cast<int>(Rp);
+    c.Cp = static_cast<int>(Cp);
+    c.n = static_cast<int>(n);
+    c.m = static_cast<int>(p.lay.m);
+    c.tall = p.lay.tall ? 1 : 0;
+    c.Tsym = pair_sym_tiles(n);
+    const int64_t M = p.lay.tall ? p.lay.m : n, N = p.lay.tall ? n : p.lay.m;
+    c.tiles_m2 = static_cast<int>((M + 255) / 256);
+    c.tiles_n = static_cast<int>((N + 255) / 256);
+    c.g0 = static_cast<int>(g0);
+    g0 += L;
+    total_per_mat[i] = static_cast<int64_t>(nsym) * c.Tsym + static_cast<int64_t>(napp) * c.tiles_m2 * c.tiles_n;
+  }
+  // Chunks: a round (every stage of one chunk per problem, skewed) should hold
+  // about two waves of pair tiles, so a tile's inputs were scheduled a round
+  // earlier; grown uniformly until the item table fits.
+  std::vector<int64_t> C(n_probs);
+  for (int i = 0; i < n_probs; ++i) {
+    C[i] = (2LL * pairs + total_per_mat[i] - 1) / total_per_mat[i];
+    if (C[i] < 1) C[i] = 1;
+    if (C[i] > probs[i].L) C[i] = probs[i].L;
+  }
+  auto count_items = [&]() {
+    int64_t items = 0;
+    for (int i = 0; i < n_probs; ++i) items += ns * ((probs[i].L + C[i] - 1) / C[i]);
+    return items;
+  };
+  while (count_items() > ps::circ::MAX_ITEMS) {
+    bool grew = false;
+    for (int i = 0; i < n_probs; ++i)
+      if (C[i] < probs[i].L) {
+        C[i] = std::min<int64_t>(probs[i].L, C[i] * 2);
+        grew = true;
+      }
+    if (!grew) return fail(PS_ERR_UNSUPPORTED, "circuit kernel: item table too large");
+  }
+  int64_t max_nch = 0;
+  for (int i = 0; i < n_probs; ++i) {
+    P.prob[i].chunk = static_cast<int>(C[i]);
+    max_nch = std::max<int64_t>(max_nch, (probs[i].L + C[i] - 1) / C[i]);
+  }
+  int items = 0;
+  int64_t tiles = 0;
+  for (int64_t round = 0; round < max_nch + ns - 1; ++round)
+    for (int i = 0; i < n_probs; ++i) {
+      const int64_t nch = (probs[i].L + C[i] - 1) / C[i];
+      for (int sg = 0; sg < ns; ++sg) {
+        const int64_t c = round - sg;
+        if (c < 0 || c >= nch) continue;
+        P.item_start[items] = static_cast<int>(tiles);
+        P.item_stage[items] = static_cast<unsigned char>(sg);
+        P.item_prob[items] = static_cast<unsigned char>(i);
+        P.item_chunk[items] = static_cast<unsigned short>(c);
+        ++items;
+        const int64_t size = std::min<int64_t>(C[i], probs[i].L - c * C[i]);
+        const int per = P.st_kind[sg] == ps::circ::kApply ? P.prob[i].tiles_m2 * P.prob[i].tiles_n
+                                                          : P.prob[i].Tsym;
+        tiles += size * per;
+      }
+    }
+  if (tiles > INT32_MAX) return fail(PS_ERR_UNSUPPORTED, "circuit kernel: too many tiles");
+  P.item_start[items] = static_cast<int>(tiles);
+  P.n_items = items;
+  P.total_tiles = static_cast<int>(tiles);
+  P.done = reinterpret_cast<unsigned*>(ws + plan.circ_off);
+  P.status = st->status;
+  P.wait_limit = g_wait_limit;
+  if (pairs > P.total_tiles) pairs = P.total_tiles;
+  cfg.gridDim = dim3(2 * pairs);
+  double flops = 0.0;
+  for (int i = 0; i < n_probs; ++i) {
+    const double n = static_cast<double>(plan.probs[i].lay.n), m = static_cast<double>(plan.probs[i].lay.m);
+    flops += probs[i].L * (n_outer * 3.0 * n * n * m + off * n * n * n);
+  }
+  LaunchScope scope(kProfCircuit, stream, flops, 0.0);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
+  if (e != cudaSuccess) return cuda_fail(e, "circuit kernel launch");
   return PS_OK;
 }
 
@@ -1570,6 +1788,13 @@ int ps_set_fused_normalize(int mode) {
     return fail(PS_ERR_INVALID, "ps_set_fused_normalize: mode must be 0 or 1");
   const int previous = g_norm_fused;
   g_norm_fused = mode;
+  return previous;
+}
+
+int ps_set_circuit_kernel(int mode) {
+  if (mode < 0 || mode > 1) return fail(PS_ERR_INVALID, "ps_set_circuit_kernel: mode must be 0 or 1");
+  const int previous = g_circuit_mode;
+  g_circuit_mode = mode;
   return previous;
 }
 
@@ -1947,6 +2172,23 @@ int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* updates,
                  (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 && aligned16(q.y));
   }
   // Chain launches count completed tiles per matrix from zero within this call.
+  if (use_circuit_kernel(plan, np, n_outer, n_steps, buffers)) {
+    // every stage of every problem in one persistent launch
+    if ((rc = circuit_kernel_run(plan, probs, updates, np, n_outer, residuals, n_steps, steps, buffers,
+                                 ws, direct, s)))
+      return rc;
+    for (int i = 0; i < np; ++i) {
+      if (direct[i]) continue;
+      const GroupedPlan::Prob& p = plan.probs[i];
+      const ps_problem& q = probs[i];
+      // the final apply wrote Xh[1 - cur], cur flipping after each of the other applies
+      const int fin = (n_outer - 1) & 1 ? 0 : 1;
+      if ((rc = copy_out(ws + p.xh_off[fin], p.lay.Rp, p.lay.Cp, q.rows, q.cols, q.L, q.y,
+                         q.y_dtype, st->sms, s)))
+        return rc;
+    }
+    return PS_OK;
+  }
   int off = 0;
   for (int t = 0; t < n_outer; ++t) {
     // The Grams of all problems, batched into one launch per kernel variant.

@@ -30,7 +30,7 @@ EXPORTED = (
     "ps_apply", "ps_add_diag", "ps_circuit_workspace_bytes", "ps_circuit",
     "ps_circuit_grouped_workspace_bytes", "ps_circuit_grouped", "ps_launch_count",
     "ps_profile_enable", "ps_profile_read", "ps_normalize_noalloc", "ps_set_cta_pairs", "ps_set_chain",
-    "ps_set_fused_normalize", "ps_circuit_grouped_update",
+    "ps_set_fused_normalize", "ps_circuit_grouped_update", "ps_set_circuit_kernel",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
     "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
 )
@@ -97,6 +97,7 @@ _SIGNATURES = {
     "ps_set_cta_pairs": ([_int], _int),
     "ps_set_chain": ([_int], _int),
     "ps_set_fused_normalize": ([_int], _int),
+    "ps_set_circuit_kernel": ([_int], _int),
     "ps_set_max_ctas": ([_int], _int),
     "ps_gns_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "ps_sumsq": ([_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr, _i64, _ptr], _int),
@@ -175,7 +176,7 @@ def selftest_wait(limit_cycles, device=None):
     check("ps_selftest_wait", load().ps_selftest_wait(int(limit_cycles), stream_ptr(device)))
 
 
-PROFILE_KINDS = {"normalize": 0, "gram": 1, "square": 2, "apply": 3, "other": 4}
+PROFILE_KINDS = {"normalize": 0, "gram": 1, "square": 2, "apply": 3, "other": 4, "circuit": 5}
 
 
 def launch_count():
@@ -215,6 +216,15 @@ def set_chain(mode):
     rc = load().ps_set_chain(int(mode))
     if rc < 0:
         check("ps_set_chain", rc)
+    return rc
+
+
+def set_circuit_kernel(mode):
+    """Grouped circuits on CTA pairs: 1 one persistent launch for all stages, 0 (default)
+    one launch per stage. Returns the previous mode."""
+    rc = load().ps_set_circuit_kernel(int(mode))
+    if rc < 0:
+        check("ps_set_circuit_kernel", rc)
     return rc
 
 

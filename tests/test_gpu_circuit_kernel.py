@@ -1,0 +1,111 @@
+"""The whole-circuit kernel (ps_set_circuit_kernel(1)): every stage of every
+problem of a grouped call -- each matrix's Gram, inner iterations and apply,
+for all outer iterations -- in one persistent CTA-pair launch, the stages of
+a matrix chained through per-matrix completion counters with bounded waits.
+
+Each tile is computed as the per-stage launches compute it, so results must
+be the same bits as the per-stage path (ps_set_circuit_kernel(0)) for every
+table shape (two and three buffers, residual applies of Polar Express, one
+to five inner iterations), wide, tall and square inputs, padded shapes whose
+final apply goes through the FP16 workspace, every output dtype, Muon updates
+folded into the last apply, and a grouped call with more problems than one
+launch takes (which falls back to per-stage launches). The per-stage path's
+parity with the oracle is tested in test_gpu_circuit.py / test_gpu_large.py.
+"""
+
+import pytest
+import torch
+
+from polar_switch import _native as nat
+from polar_switch import make_polynomial_orthogonalizer
+from tests._util import seeded
+
+pytestmark = pytest.mark.gpu
+
+
+def _both(fn):
+    """fn() with the whole-circuit kernel, then with per-stage launches."""
+    prev = nat.set_circuit_kernel(1)
+    try:
+        on = fn()
+        torch.cuda.synchronize()
+        nat.set_circuit_kernel(0)
+        off = fn()
+        torch.cuda.synchronize()
+    finally:
+        nat.set_circuit_kernel(prev)
+    return on, off
+
+
+def _banks(shapes, seed, dtype=torch.float32, device="cuda"):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(*s, generator=g).to(dtype).to(device) for s in shapes]
+
+
+CASES = [
+    ("PS2_55", torch.float32, [(1, 2048, 1024), (2, 1024, 1024), (1, 1024, 2048), (2, 3072, 1024),
+                               (1, 1024, 3072)]),
+    ("PS3_55", torch.bfloat16, [(6, 768, 768), (2, 768, 3072), (2, 3072, 768)]),
+    ("PS2_55", torch.float16, [(30, 256, 256), (3, 128, 640)]),
+    ("POLAR_EXPRESS", torch.float32, [(3, 384, 512), (2, 512, 256)]),
+    ("PS3_55", torch.float32, [(3, 130, 66), (2, 200, 136)]),   # padded: final apply via Xh
+    ("PS2_64", torch.float32, [(1, 2048, 2048)]),
+    ("PS2_11111", torch.float32, [(4, 256, 640)]),
+]
+
+
+@pytest.mark.parametrize("method,dtype,shapes", CASES,
+                         ids=[f"{m}-{str(d)[6:]}-{len(s)}" for m, d, s in CASES])
+def test_circuit_kernel_equals_per_stage_launches(cuda_device, method, dtype, shapes):
+    banks = _banks(shapes, 21, dtype, cuda_device)
+    polar = make_polynomial_orthogonalizer(method)
+    on, off = _both(lambda: polar.grouped(banks))
+    for a, b, s in zip(on, off, shapes):
+        assert a.dtype == dtype and torch.equal(a, b), f"{method} {s}: circuit kernel differs"
+    assert nat.get_status() == 0
+
+
+def test_circuit_kernel_single_call_and_launch_count(cuda_device):
+    X = seeded((4, 512, 1024), 22).to(cuda_device)
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    on, off = _both(lambda: polar(X))
+    assert torch.equal(on, off)
+    prev = nat.set_circuit_kernel(1)
+    try:
+        n0 = nat.launch_count()
+        nat.profile_enable(True)
+        polar(X)
+        prof = nat.profile_read()
+        nat.profile_enable(False)
+    finally:
+        nat.set_circuit_kernel(prev)
+    # two normalisation passes and one launch for the whole circuit
+    assert nat.launch_count() - n0 == 3
+    assert prof["circuit"]["launches"] == 1 and prof["square"]["launches"] == 0
+    assert prof["circuit"]["flops"] == pytest.approx(4 * (22 * 512 ** 3))
+
+
+def test_circuit_kernel_with_folded_muon_update(cuda_device):
+    shapes = [(3, 256, 512), (2, 384, 128), (4, 192, 192)]
+    dirs = _banks(shapes, 23, torch.bfloat16, cuda_device)
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    base = _banks(shapes, 24, torch.float32, cuda_device)
+    factors = [(0.998, -0.013), (0.999, -0.02), (1.0, -0.007)]
+
+    def run():
+        banks = [b.clone() for b in base]
+        polar.grouped(dirs, updates=[(b, d, a) for b, (d, a) in zip(banks, factors)])
+        return banks
+
+    on, off = _both(run)
+    for a, b in zip(on, off):
+        assert torch.equal(a, b)
+
+
+def test_more_problems_than_one_launch_fall_back(cuda_device):
+    shapes = [(1, 128, 128 + 64 * i) for i in range(10)]  # 10 problems > 8 per launch
+    banks = _banks(shapes, 25, torch.float32, cuda_device)
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    on, off = _both(lambda: polar.grouped(banks))
+    for a, b in zip(on, off):
+        assert torch.equal(a, b)

@@ -118,3 +118,11 @@ def test_fused_normalize_knob_without_gpu():
     prev = lib.ps_set_fused_normalize(1)
     assert prev == 0  # default: two passes
     assert lib.ps_set_fused_normalize(prev) == 1
+
+
+def test_circuit_kernel_knob_without_gpu():
+    lib = _native.load()
+    assert lib.ps_set_circuit_kernel(2) == _native.PS_ERR_INVALID
+    prev = lib.ps_set_circuit_kernel(1)
+    assert prev in (0, 1)
+    assert lib.ps_set_circuit_kernel(prev) == 1
