@@ -308,7 +308,16 @@ def run_kernel(args):
     device = torch.device("cuda", 0)
     shapes = bank_shapes(args.workload)
     g = torch.Generator(device=device).manual_seed(0)
-    if args.kernel == "chain":
+    if args.kernel == "circuit":
+        # the whole-circuit kernel on the workload's banks (one launch per call)
+        from polar_switch import make_polynomial_orthogonalizer
+        L0 = args.L or None
+        banks = [torch.randn(L0 or L, r, c, generator=g, device=device) for L, r, c in shapes]
+        polar = make_polynomial_orthogonalizer(WORKLOADS[args.workload]["method"])
+        nat.set_circuit_kernel(1)
+        fn = lambda: polar.grouped(banks)  # noqa: E731
+        desc = f"circuit ({WORKLOADS[args.workload]['method']}) banks {[tuple(b.shape) for b in banks]}"
+    elif args.kernel == "chain":
         # all inner iterations of the workload's squares as the circuit runs
         # them: whole PS2-55 circuits on L square matrices of the bank's n
         from polar_switch import make_polynomial_orthogonalizer
@@ -317,6 +326,7 @@ def run_kernel(args):
         X = torch.randn(L, n, n, generator=g, device=device)
         Y = torch.empty_like(X)
         polar = make_polynomial_orthogonalizer("PS2_55")
+        nat.set_circuit_kernel(0)  # per-stage launches: the chain runs the inner iterations
         fn = lambda: polar(X, out=Y)  # noqa: E731
         desc = f"chain (PS2_55 circuits) L={L} n={n}"
     elif args.kernel in ("square", "sym_product"):
@@ -507,7 +517,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-single", dest="single", action="store_false",
                     help="skip the 8192 x 8192 PS2-55 point timed after the step at N = 1")
-    ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize", "chain"],
+    ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize", "chain",
+                                         "circuit"],
                     help="time one kernel class alone (for profiling) instead of the whole step")
     ap.add_argument("--bank", type=int, default=0, help="bank of the workload used by --kernel")
     ap.add_argument("--L", type=int, default=0, help="--kernel: override the number of matrices")

@@ -137,10 +137,10 @@ PS_API int ps_set_cta_pairs(int mode);
  * kernel per inner iteration). */
 PS_API int ps_set_chain(int mode);
 
-/* How ps_circuit / ps_circuit_grouped run on the CTA-pair path: 1 = one
- * persistent launch for every stage of every problem (each matrix's Gram,
+/* How ps_circuit / ps_circuit_grouped run on the CTA-pair path: 1 (default) =
+ * one persistent launch for every stage of every problem (each matrix's Gram,
  * inner iterations and apply chained through per-matrix completion counters,
- * bounded waits), 0 (default) = one launch per stage. Same bits either way;
+ * bounded waits), 0 = one launch per stage. Same bits either way;
  * up to 8 problems, 3 buffers and 48 stages (else per-stage launches).
  * Returns the previous mode (PS_ERR_INVALID for other values). Replaces the
  * whole loop of polar_switch/__init__.py:40-44 with one launch. */

@@ -220,7 +220,7 @@ def set_chain(mode):
 
 
 def set_circuit_kernel(mode):
-    """Grouped circuits on CTA pairs: 1 one persistent launch for all stages, 0 (default)
+    """Grouped circuits on CTA pairs: 1 (default) one persistent launch for all stages, 0
     one launch per stage. Returns the previous mode."""
     rc = load().ps_set_circuit_kernel(int(mode))
     if rc < 0:

@@ -25,6 +25,16 @@ from tests._util import seeded
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def per_stage_launches():
+    """The chain is the inner-iteration launch of the per-stage path; the
+    whole-circuit kernel (the default) replaces it, so these tests run with
+    per-stage launches."""
+    prev = nat.set_circuit_kernel(0)
+    yield
+    nat.set_circuit_kernel(prev)
+
+
 def _both(fn):
     """fn() with the chain on, then off; restores the previous mode."""
     prev = nat.set_chain(1)

@@ -233,6 +233,7 @@ def test_launch_counter_and_profiler(cuda_device):
     from polar_switch import make_polynomial_orthogonalizer
     polar = make_polynomial_orthogonalizer("PS2_55")
     X = seeded((2, 256, 512), 61).to(cuda_device)
+    prev_circ = nat.set_circuit_kernel(0)  # per-stage launches, counted below
     for chain, squares in ((0, 10), (1, 2)):
         prev = nat.set_chain(chain)
         try:
@@ -250,3 +251,4 @@ def test_launch_counter_and_profiler(cuda_device):
         assert prof["apply"]["launches"] == 2
         assert prof["square"]["flops"] == pytest.approx(10 * 2 * 256 ** 3)
         assert all(v["ms"] > 0 for v in prof.values() if v["launches"])
+    nat.set_circuit_kernel(prev_circ)
