@@ -529,8 +529,10 @@ def main():
                     help="multi-GPU: cap on GEMM CTAs, leaving SMs to the all-gather")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="enqueue every step from the host instead of replaying a CUDA graph of it")
-    ap.add_argument("--transport", default="auto", choices=["auto", "copy_engine", "collective"],
-                    help="multi-GPU: copy-engine pushes into symmetric memory, or the NCCL all-gather")
+    ap.add_argument("--transport", default="auto", choices=["auto", "push", "copy_engine", "collective"],
+                    help="multi-GPU: result tiles stored into the peers' symmetric memory from inside "
+                         "the circuit launch (push; auto when it fits), copy-engine pushes into "
+                         "symmetric memory, or the NCCL all-gather")
     ap.add_argument("--sweep", action="store_true",
                     help="median circuit latency on every shape with a published reference latency")
     ap.add_argument("--methods", default="PS2_55,PS3_55,GNS", help="--sweep: methods to time")
@@ -684,6 +686,7 @@ def main():
         line["config"]["cuda_graph"] = bool(args.graph)
         if world > 1:
             line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
+                                        "phases": getattr(step, "phase_fractions", None),
                                         "split_matrices": type(step).__name__ == "SplitOrthogonalizer",
                                         "gemm_ctas": args.gemm_ctas,
                                         "bucket_matrices": [sum(c for _, _, c in p["pieces"]) for p in step.plans],

@@ -298,6 +298,34 @@ PS_API int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* u
                                      const ps_step* steps, int buffers, float eps, void* workspace,
                                      int64_t workspace_bytes, void* stream);
 
+/* ps_circuit_grouped in one whole-circuit launch whose final results are
+ * also stored straight into other GPUs' memory: the all-gather after a
+ * sharded orthogonalization (train_nanogpt.py:4025-4037, each rank's updates
+ * all-gathered after its local orthogonalization) fused into the last
+ * apply's epilogue, tile by tile, while later matrices still compute.
+ *
+ * Every y lies inside one buffer that starts at local_base on this GPU and
+ * whose copy on peer k (the same layout) starts at peer_bases[k], a device
+ * address this GPU can store to (a peer's symmetric-memory buffer); each
+ * final tile is stored to y and to peer_bases[k] + (y - local_base) for k <
+ * n_peers (at most 7). The stores are complete when the kernel has finished;
+ * ordering them against the peers' use of their buffers (a barrier before and
+ * after the call) is the caller's. n_phases (1..8) groups each problem's
+ * matrices: phase_ends[i * n_phases + k] is the number of problem i's matrices
+ * in phases 0..k (non-decreasing, the last equal to its L; NULL when
+ * n_phases == 1); the tiles of a phase are scheduled before those of the
+ * next, so its results reach the peers while later phases compute. The bits
+ * stored are ps_circuit_grouped's. Needs the whole-circuit kernel (at most 8
+ * problems, ps_set_circuit_kernel(1)) and rows and cols multiples of 8 with
+ * 16-byte aligned y and 16-byte rows; PS_ERR_UNSUPPORTED otherwise, before
+ * anything is launched. */
+PS_API int ps_circuit_grouped_push(const ps_problem* probs, int n_probs, int n_outer,
+                                   const float* residuals, const int32_t* n_steps,
+                                   const ps_step* steps, int buffers, float eps, void* workspace,
+                                   int64_t workspace_bytes, const void* local_base,
+                                   const void* const* peer_bases, int n_peers, int n_phases,
+                                   const int32_t* phase_ends, void* stream);
+
 /* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 

@@ -1410,8 +1410,25 @@ bool use_circuit_kernel(const GroupedPlan& plan, int n_probs, int n_outer, const
   if (stages > ps::circ::MAX_STAGES || steps > ps::circ::MAX_STEPS) return false;
   for (const GroupedPlan::Prob& p : plan.probs)
     if (!use_pair(true, p.lay.n) || !use_pair(false, p.lay.n)) return false;
+  // the item table indexes matrices with 16 bits
+  for (const GroupedPlan::NGroup& g : plan.groups)
+    if (g.Ltot > 65535) return false;
   return true;
 }
+
+// Where a whole-circuit launch also stores its final results (other GPUs'
+// copies of the buffer holding every y, at peer_bases[k] for the buffer at
+// local_base here) and how its matrices are ordered: phase_ends[i * n_phases +
+// k] is the number of problem i's matrices in phases 0..k; the tiles of a
+// phase are scheduled before those of the next, so its results are final
+// (and pushed) while later phases compute. No push and one phase: nullptr.
+struct CircuitPush {
+  const uint8_t* local_base = nullptr;
+  const void* const* peer_bases = nullptr;
+  int n_peers = 0;
+  int n_phases = 1;
+  const int32_t* phase_ends = nullptr;
+};
 
 // All stages of a grouped circuit in one launch (ps_circuit.cuh). `cur0` is
 // the Xh buffer holding the normalised inputs; the final applies store into
@@ -1419,7 +1436,7 @@ bool use_circuit_kernel(const GroupedPlan& plan, int n_probs, int n_outer, const
 int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const ps_update* updates,
                        int n_probs, int n_outer, const float* residuals, const int32_t* n_steps,
                        const ps_step* steps, int buffers, uint8_t* ws, const std::vector<bool>& direct,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const CircuitPush* push = nullptr) {
   using ps::circ::CircuitParams;
   DeviceState* st = nullptr;
   int rc = device_state(&st);
@@ -1512,6 +1529,14 @@ int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const p
     c.y_out = q.y_dtype == PS_F32 ? ps::kOutF32 : q.y_dtype == PS_BF16 ? ps::kOutBF16 : ps::kOutF16;
     if (direct[i] && !upd) {
       if ((rc = map_out(&c.yo, q.y, q.y_dtype, q.cols, q.rows, L, q.cols, q.rows * q.cols))) return rc;
+      if (push)
+        for (int k = 0; k < push->n_peers; ++k) {
+          const uint8_t* peer_y = static_cast<const uint8_t*>(push->peer_bases[k]) +
+                                  (static_cast<const uint8_t*>(q.y) - push->local_base);
+          if ((rc = map_out(&P.ypeer[i][k], peer_y, q.y_dtype, q.cols, q.rows, L, q.cols,
+                            q.rows * q.cols)))
+            return rc;
+        }
     }
     if (upd) {
       c.upd = 1;
@@ -1538,15 +1563,25 @@ int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const p
   // Chunks: a round (every stage of one chunk per problem, skewed) should hold
   // about two waves of pair tiles, so a tile's inputs were scheduled a round
   // earlier; grown uniformly until the item table fits.
+  // Phases (push): matrices [begin(i, k), end(i, k)) of problem i in phase k.
+  const int n_phases = push ? push->n_phases : 1;
+  auto phase_begin = [&](int i, int k) -> int64_t {
+    return k == 0 ? 0 : static_cast<int64_t>(push->phase_ends[i * n_phases + k - 1]);
+  };
+  auto phase_end = [&](int i, int k) -> int64_t {
+    return n_phases == 1 ? probs[i].L : static_cast<int64_t>(push->phase_ends[i * n_phases + k]);
+  };
   std::vector<int64_t> C(n_probs);
   for (int i = 0; i < n_probs; ++i) {
     C[i] = (2LL * pairs + total_per_mat[i] - 1) / total_per_mat[i];
     if (C[i] < 1) C[i] = 1;
     if (C[i] > probs[i].L) C[i] = probs[i].L;
   }
+  auto chunks_of = [&](int i, int k) { return (phase_end(i, k) - phase_begin(i, k) + C[i] - 1) / C[i]; };
   auto count_items = [&]() {
     int64_t items = 0;
-    for (int i = 0; i < n_probs; ++i) items += ns * ((probs[i].L + C[i] - 1) / C[i]);
+    for (int k = 0; k < n_phases; ++k)
+      for (int i = 0; i < n_probs; ++i) items += ns * chunks_of(i, k);
     return items;
   };
   while (count_items() > ps::circ::MAX_ITEMS) {
@@ -1558,30 +1593,32 @@ int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const p
       }
     if (!grew) return fail(PS_ERR_UNSUPPORTED, "circuit kernel: item table too large");
   }
-  int64_t max_nch = 0;
-  for (int i = 0; i < n_probs; ++i) {
-    P.prob[i].chunk = static_cast<int>(C[i]);
-    max_nch = std::max<int64_t>(max_nch, (probs[i].L + C[i] - 1) / C[i]);
-  }
+  for (int i = 0; i < n_probs; ++i) P.prob[i].chunk = static_cast<int>(C[i]);
   int items = 0;
   int64_t tiles = 0;
-  for (int64_t round = 0; round < max_nch + ns - 1; ++round)
-    for (int i = 0; i < n_probs; ++i) {
-      const int64_t nch = (probs[i].L + C[i] - 1) / C[i];
-      for (int sg = 0; sg < ns; ++sg) {
-        const int64_t c = round - sg;
-        if (c < 0 || c >= nch) continue;
-        P.item_start[items] = static_cast<int>(tiles);
-        P.item_stage[items] = static_cast<unsigned char>(sg);
-        P.item_prob[items] = static_cast<unsigned char>(i);
-        P.item_chunk[items] = static_cast<unsigned short>(c);
-        ++items;
-        const int64_t size = std::min<int64_t>(C[i], probs[i].L - c * C[i]);
-        const int per = P.st_kind[sg] == ps::circ::kApply ? P.prob[i].tiles_m2 * P.prob[i].tiles_n
-                                                          : P.prob[i].Tsym;
-        tiles += size * per;
+  for (int k = 0; k < n_phases; ++k) {
+    int64_t max_nch = 0;
+    for (int i = 0; i < n_probs; ++i) max_nch = std::max<int64_t>(max_nch, chunks_of(i, k));
+    for (int64_t round = 0; round < max_nch + ns - 1; ++round)
+      for (int i = 0; i < n_probs; ++i) {
+        const int64_t nch = chunks_of(i, k), b0 = phase_begin(i, k), b1 = phase_end(i, k);
+        for (int sg = 0; sg < ns; ++sg) {
+          const int64_t c = round - sg;
+          if (c < 0 || c >= nch) continue;
+          const int64_t first = b0 + c * C[i];
+          P.item_start[items] = static_cast<int>(tiles);
+          P.item_stage[items] = static_cast<unsigned char>(sg);
+          P.item_prob[items] = static_cast<unsigned char>(i);
+          P.item_first[items] = static_cast<unsigned short>(first);
+          ++items;
+          const int64_t size = std::min<int64_t>(C[i], b1 - first);
+          const int per = P.st_kind[sg] == ps::circ::kApply ? P.prob[i].tiles_m2 * P.prob[i].tiles_n
+                                                            : P.prob[i].Tsym;
+          tiles += size * per;
+        }
       }
-    }
+  }
+  if (push) P.n_peers = push->n_peers;
   if (tiles > INT32_MAX) return fail(PS_ERR_UNSUPPORTED, "circuit kernel: too many tiles");
   P.item_start[items] = static_cast<int>(tiles);
   P.n_items = items;
@@ -2099,10 +2136,64 @@ int ps_circuit_grouped(const ps_problem* probs, int n_probs, int n_outer, const 
                                    buffers, eps, workspace, workspace_bytes, stream);
 }
 
+static int circuit_grouped_impl(const ps_problem* probs, const ps_update* updates, int n_probs,
+                                int n_outer, const float* residuals, const int32_t* n_steps,
+                                const ps_step* steps, int buffers, float eps, void* workspace,
+                                int64_t workspace_bytes, void* stream, const CircuitPush* push);
+
 int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* updates, int n_probs,
                               int n_outer, const float* residuals, const int32_t* n_steps,
                               const ps_step* steps, int buffers, float eps, void* workspace,
                               int64_t workspace_bytes, void* stream) {
+  return circuit_grouped_impl(probs, updates, n_probs, n_outer, residuals, n_steps, steps, buffers,
+                              eps, workspace, workspace_bytes, stream, nullptr);
+}
+
+int ps_circuit_grouped_push(const ps_problem* probs, int n_probs, int n_outer, const float* residuals,
+                            const int32_t* n_steps, const ps_step* steps, int buffers, float eps,
+                            void* workspace, int64_t workspace_bytes, const void* local_base,
+                            const void* const* peer_bases, int n_peers, int n_phases,
+                            const int32_t* phase_ends, void* stream) {
+  if (n_peers < 0 || n_peers > ps::circ::MAX_PEERS)
+    return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: n_peers must be in [0, %d]",
+                ps::circ::MAX_PEERS);
+  if (n_peers > 0 && (!local_base || !peer_bases))
+    return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: null local_base or peer_bases");
+  for (int k = 0; k < n_peers; ++k)
+    if (!peer_bases[k] || !aligned16(peer_bases[k]))
+      return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: peer base %d is null or misaligned", k);
+  if (n_phases < 1 || n_phases > ps::circ::MAX_PHASES)
+    return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: n_phases must be in [1, %d]",
+                ps::circ::MAX_PHASES);
+  if (!probs || n_probs <= 0) return fail(PS_ERR_INVALID, "ps_circuit: bad problem list");
+  if (n_phases > 1) {
+    if (!phase_ends) return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: null phase_ends");
+    for (int i = 0; i < n_probs; ++i) {
+      int32_t prev = 0;
+      for (int k = 0; k < n_phases; ++k) {
+        const int32_t e = phase_ends[i * n_phases + k];
+        if (e < prev || (k == n_phases - 1 && e != probs[i].L))
+          return fail(PS_ERR_INVALID,
+                      "ps_circuit_grouped_push: phase_ends of problem %d must be non-decreasing "
+                      "and end at its L", i);
+        prev = e;
+      }
+    }
+  }
+  CircuitPush push;
+  push.local_base = static_cast<const uint8_t*>(local_base);
+  push.peer_bases = peer_bases;
+  push.n_peers = n_peers;
+  push.n_phases = n_phases;
+  push.phase_ends = n_phases > 1 ? phase_ends : nullptr;
+  return circuit_grouped_impl(probs, nullptr, n_probs, n_outer, residuals, n_steps, steps, buffers,
+                              eps, workspace, workspace_bytes, stream, &push);
+}
+
+static int circuit_grouped_impl(const ps_problem* probs, const ps_update* updates, int n_probs,
+                                int n_outer, const float* residuals, const int32_t* n_steps,
+                                const ps_step* steps, int buffers, float eps, void* workspace,
+                                int64_t workspace_bytes, void* stream, const CircuitPush* push) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (!workspace) return fail(PS_ERR_INVALID, "ps_circuit: null workspace");
   if (!probs || n_probs <= 0) return fail(PS_ERR_INVALID, "ps_circuit: bad problem list");
@@ -2155,6 +2246,24 @@ int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* updates,
                     p.lay.Rp, p.lay.Cp, reinterpret_cast<double*>(ws + p.norm_off),
                     reinterpret_cast<unsigned*>(ws + p.cnt_off)};
   }
+  if (push) {
+    // Checked before anything is launched, so a caller can take another path.
+    if (!use_circuit_kernel(plan, np, n_outer, n_steps, buffers))
+      return fail(PS_ERR_UNSUPPORTED,
+                  "ps_circuit_grouped_push: the problems do not fit one whole-circuit launch");
+    for (int i = 0; i < np; ++i) {
+      const ps_problem& q = probs[i];
+      const GroupedPlan::Prob& p = plan.probs[i];
+      if (!((q.y_dtype == PS_F16 || q.y_dtype == PS_F32 || q.y_dtype == PS_BF16) &&
+            p.lay.Rp == q.rows && p.lay.Cp == q.cols && (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 &&
+            aligned16(q.y)))
+        return fail(PS_ERR_UNSUPPORTED,
+                    "ps_circuit_grouped_push: problem %d needs rows and cols multiples of 8 and a "
+                    "16-byte aligned y with 16-byte rows", i);
+      if (push->n_peers > 0 && static_cast<const uint8_t*>(q.y) < push->local_base)
+        return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: y of problem %d lies before local_base", i);
+    }
+  }
   std::vector<unsigned> chain_base(plan.groups.size(), 0u);
   {
     // chain and fused-normalisation counters start at zero in every call
@@ -2177,7 +2286,7 @@ int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* updates,
   if (use_circuit_kernel(plan, np, n_outer, n_steps, buffers)) {
     // every stage of every problem in one persistent launch
     if ((rc = circuit_kernel_run(plan, probs, updates, np, n_outer, residuals, n_steps, steps, buffers,
-                                 ws, direct, s)))
+                                 ws, direct, s, push)))
       return rc;
     for (int i = 0; i < np; ++i) {
       if (direct[i]) continue;

@@ -30,6 +30,8 @@ constexpr int MAXB = 3;         // square buffers
 constexpr int MAX_STAGES = 48;  // stages per matrix (Gram, inner iterations, apply per outer)
 constexpr int MAX_STEPS = 40;   // inner iterations over all outer iterations
 constexpr int MAX_ITEMS = 768;  // (stage, problem, chunk) items
+constexpr int MAX_PEERS = 7;    // other GPUs a final result is also stored to
+constexpr int MAX_PHASES = 8;   // groups of matrices scheduled one after another
 constexpr int SIGNALS_PER_TILE = 2 * pair::NUM_EPI_WARPS;
 
 enum Kind : int { kGram = 0, kSquare = 1, kApply = 2 };
@@ -69,9 +71,16 @@ struct alignas(64) CircuitParams {
   int* status;
   long long wait_limit;
   int item_start[MAX_ITEMS + 1];
-  unsigned short item_chunk[MAX_ITEMS];
+  unsigned short item_first[MAX_ITEMS];  // first matrix (within its problem) of the item's chunk
   unsigned char item_stage[MAX_ITEMS], item_prob[MAX_ITEMS];
+  // Push: every tile a final apply stores into y is also stored, through
+  // ypeer[p][k] (y's layout at another GPU's address), into n_peers other
+  // GPUs' memory. A final apply has no dependent stage, so pushed tiles are
+  // not published on the counters; their stores complete by kernel exit.
+  int n_peers;
+  CUtensorMap ypeer[MAXP][MAX_PEERS];
 };
+static_assert(sizeof(CircuitParams) <= 32764, "kernel parameter space");
 
 struct Tile {
   int kind, p, b, t, s;  // stage kind, problem, matrix, outer iteration, step index
@@ -98,7 +107,7 @@ __device__ __forceinline__ void decode(const CircuitParams& P, int t, uint32_t r
   const int local = t - P.item_start[lo];
   const int mat = local / per;
   int r = local - mat * per;
-  d.b = P.item_chunk[lo] * q.chunk + mat;
+  d.b = P.item_first[lo] + mat;
   d.need = sg == 0 ? 0u
                    : static_cast<unsigned>(SIGNALS_PER_TILE) *
                          (static_cast<unsigned>(P.st_nsym[sg]) * q.Tsym +
@@ -447,6 +456,7 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
         }
       }
       const bool upd = final_apply && q.direct && q.upd;
+      const bool push = final_apply && q.direct && !q.upd && P.n_peers > 0;
       const int c_first = 4 * h;
       int nvalid = N - (d.n0 + 32 * c_first);
       nvalid = nvalid > 128 ? 128 : nvalid;
@@ -549,7 +559,11 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (row0 < M && gcol0 < N) tma_store_3d(tmD, sb, gcol0, row0, d.b);
+          if (row0 < M && gcol0 < N) {
+            tma_store_3d(tmD, sb, gcol0, row0, d.b);
+            if (push)
+              for (int k = 0; k < P.n_peers; ++k) tma_store_3d(&P.ypeer[d.p][k], sb, gcol0, row0, d.b);
+          }
           bulk_commit();
         }
         slot = (slot_bytes == 4096) ? 0 : (slot ^ 1);
@@ -603,8 +617,9 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
           }
         }
       }
-      // Publish this warp's part of the tile (stores complete and visible).
-      if (lane == 0) {
+      // Publish this warp's part of the tile (stores complete and visible);
+      // pushed final tiles have no reader in this launch.
+      if (lane == 0 && !push) {
         bulk_wait<0>();
         fence_proxy_async_global();
         red_release_gpu_add_u32(P.done + q.g0 + d.b, 1u);

@@ -132,7 +132,7 @@ class _Circuit:
         return out
 
 
-    def grouped(self, banks, epsilon, outs=None, updates=None):
+    def grouped(self, banks, epsilon, outs=None, updates=None, push=None):
         """Run the circuit on several tensors of different shapes in one C call.
 
         Tensors that share n = min(rows, cols) have their inner iterations
@@ -146,6 +146,16 @@ class _Circuit:
         rounded as torch's ``p.mul_(decay); p.add_(u.to(p.dtype), alpha)``) to
         the contiguous bank of the input's shape, inside the last apply
         (ps_circuit_grouped_update). Its entry in the returned list is None.
+
+        ``push``: optional dict ``{"local": int, "peers": [int, ...],
+        "phase_ends": [[int, ...], ...]}``: every output lies in a buffer
+        starting at device address ``local`` whose copies on other GPUs start
+        at ``peers``; the final results are also stored there, tile by tile,
+        inside the circuit's one launch (ps_circuit_grouped_push), the
+        matrices of each input scheduled in the phases ``phase_ends[i]``
+        (cumulative counts ending at the input's matrix count). Raises
+        NativeError (PS_ERR_UNSUPPORTED, before anything ran) when the inputs
+        do not fit that launch.
         """
         if not banks:
             return []
@@ -187,7 +197,22 @@ class _Circuit:
             if ws_bytes < 0:
                 nat.check("ps_circuit_grouped_workspace_bytes", nat.PS_ERR_INVALID)
             ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8)
-            if upd is None:
+            if push is not None:
+                if upd is not None:
+                    raise ValueError("push and updates cannot be combined")
+                peers = [int(p) for p in push.get("peers", ())]
+                ends = push.get("phase_ends")
+                n_phases = len(ends[0]) if ends else 1
+                if ends and any(len(e) != n_phases for e in ends):
+                    raise ValueError("every input needs the same number of phases")
+                flat = [int(v) for e in ends for v in e] if ends else []
+                nat.check("ps_circuit_grouped_push", lib.ps_circuit_grouped_push(
+                    probs, len(banks), self.n_outer, self.residuals, self.n_steps, self.steps,
+                    self.buffers, float(epsilon), nat.ptr(ws), ws_bytes, push.get("local"),
+                    (ctypes.c_void_p * max(1, len(peers)))(*peers), len(peers), n_phases,
+                    (ctypes.c_int32 * max(1, len(flat)))(*flat) if flat else None,
+                    nat.stream_ptr(device)))
+            elif upd is None:
                 nat.check("ps_circuit_grouped", lib.ps_circuit_grouped(
                     probs, len(banks), self.n_outer, self.residuals, self.n_steps, self.steps,
                     self.buffers, float(epsilon), nat.ptr(ws), ws_bytes, nat.stream_ptr(device)))
@@ -257,13 +282,14 @@ def make_polynomial_orthogonalizer(method, compile=True, epsilon=1e-7):
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
 
-    def grouped(tensors, outs=None, updates=None):
+    def grouped(tensors, outs=None, updates=None, push=None):
         """Orthogonalize a list of tensors of different shapes in one grouped call
-        (``updates``: fold Muon's update of a parameter bank into the last apply,
-        see _Circuit.grouped)."""
+        (``updates``: fold Muon's update of a parameter bank into the last apply;
+        ``push``: also store the results into other GPUs' buffers from inside
+        the circuit's launch; see _Circuit.grouped)."""
         for X in tensors:
             _check_input(X)
-        result = circuit.grouped(list(tensors), epsilon, outs=outs, updates=updates)
+        result = circuit.grouped(list(tensors), epsilon, outs=outs, updates=updates, push=push)
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
 

@@ -33,6 +33,7 @@ EXPORTED = (
     "ps_set_fused_normalize", "ps_circuit_grouped_update", "ps_set_circuit_kernel",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
     "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
+    "ps_circuit_grouped_push",
 )
 
 
@@ -120,6 +121,10 @@ _SIGNATURES = {
     "ps_circuit_grouped_update": ([ctypes.POINTER(PsProblem), ctypes.POINTER(PsUpdate), _int, _int,
                                    ctypes.POINTER(_f32), ctypes.POINTER(ctypes.c_int32),
                                    ctypes.POINTER(PsStep), _int, _f32, _ptr, _i64, _ptr], _int),
+    "ps_circuit_grouped_push": ([ctypes.POINTER(PsProblem), _int, _int, ctypes.POINTER(_f32),
+                                 ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep), _int, _f32,
+                                 _ptr, _i64, _ptr, ctypes.POINTER(_ptr), _int, _int,
+                                 ctypes.POINTER(ctypes.c_int32), _ptr], _int),
 }
 
 

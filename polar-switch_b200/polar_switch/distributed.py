@@ -135,6 +135,37 @@ def simulate_buckets(fractions, compute_s, gather_s, overhead_s=BUCKET_OVERHEAD_
     return t_gather
 
 
+def phase_ends(counts, fractions):
+    """Cumulative per-phase matrix counts of each input for a push launch.
+
+    counts: matrices of each input; fractions: relative phase sizes. Returns
+    one list per input, non-decreasing, ending at its count (phases may be
+    empty for small inputs)."""
+    total = float(sum(fractions))
+    cum, acc = [], 0.0
+    for f in fractions:
+        acc += f
+        cum.append(acc / total)
+    out = []
+    for c in counts:
+        e = [min(c, max(0, int(round(c * x)))) for x in cum]
+        e[-1] = c
+        for j in range(1, len(e)):
+            e[j] = max(e[j], e[j - 1])
+        out.append(e)
+    return out
+
+
+# Push transport: phases of the rank's matrices inside its one launch. With
+# two ranks the step is compute-bound (each GPU receives half the updates
+# while computing the other half) and one phase is best; from four ranks on
+# the NVLink receive time exceeds the circuits and three equal phases put the
+# first results on the links early (modelled on the whole-circuit kernel's
+# schedule and measured on B200).
+def push_phase_fractions(world_size):
+    return [1.0] if world_size <= 2 else [1.0, 1.0, 1.0]
+
+
 def auto_bucket_fractions(banks, world_size, flops_fn):
     """Bucket cost fractions for overlapping the gather with the circuits.
 
@@ -184,7 +215,13 @@ class ShardedOrthogonalizer:
         buffer, a symmetric-memory allocation, with peer-to-peer copies that
         run on the copy engines and leave every SM to the circuits),
         "collective" (an asynchronous all_gather_into_tensor of the group's
-        backend) or "auto" (copy engines on CUDA, else the collective)."""
+        backend), "push" (one launch per rank for all its matrices, whose last
+        apply stores every result tile into every peer's receive buffer as it
+        is computed: the gather fused into the circuit; ``buckets`` then
+        give the phases the launch schedules one after another, by default
+        `push_phase_fractions`) or "auto" (push on CUDA when the rank's work
+        fits one whole-circuit launch, else copy engines; the collective off
+        CUDA)."""
         self.group = group
         if world_size is None:
             world_size = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -198,6 +235,16 @@ class ShardedOrthogonalizer:
         table = self.polar.table
         self.flops_fn = lambda r, c: circuit_flops(table, r, c)
         self.bank_shapes = [tuple(int(v) for v in s) for s in bank_shapes]
+        if transport not in ("auto", "copy_engine", "collective", "push"):
+            raise ValueError(f"unknown transport {transport!r}")
+        if transport == "auto" and world_size > 1 and self.native_circuit and torch.device(
+                device if device is not None else "cuda").type == "cuda" and self._push_fits():
+            transport = "push"
+        self.phase_fractions = None
+        if transport == "push":
+            self.phase_fractions = (push_phase_fractions(world_size) if buckets is None else
+                                    [1.0] * buckets if isinstance(buckets, int) else list(buckets))
+            buckets = 1
         if buckets is None:
             buckets = 1 if world_size == 1 else auto_bucket_fractions(self.bank_shapes, world_size,
                                                                        self.flops_fn)
@@ -219,15 +266,13 @@ class ShardedOrthogonalizer:
             offset += world_size * seg
         # In-place gathers: this rank's segment of each bucket's receive region
         # is its send buffer, so the circuit writes results where they end up.
-        if transport not in ("auto", "copy_engine", "collective"):
-            raise ValueError(f"unknown transport {transport!r}")
         if transport == "auto":
             transport = "copy_engine" if world_size > 1 and self.device.type == "cuda" else "collective"
         if world_size == 1:
             transport = "none"
         self.transport = transport
         numel = max(offset, 1)
-        if transport == "copy_engine":
+        if transport in ("copy_engine", "push"):
             import torch.distributed._symmetric_memory as symm
             self.recv = symm.empty(numel, device=self.device, dtype=torch.float16)
             handle = symm.rendezvous(self.recv, self.group if self.group is not None else dist.group.WORLD)
@@ -235,6 +280,14 @@ class ShardedOrthogonalizer:
             self._handle = handle
             self._comm = torch.cuda.Stream(device=self.device)
             self._flag = torch.zeros(1, device=self.device, dtype=torch.int32)
+            self._push_unsupported = False
+            if transport == "push":
+                plan = self.plans[0]
+                counts = [v.shape[0] for _, _, v in self._segment_views(plan, self.rank)]
+                self._push = {"local": self.recv.data_ptr(),
+                              "peers": [self._peer_recv[p].data_ptr() for p in range(world_size)
+                                        if p != rank],
+                              "phase_ends": phase_ends(counts, self.phase_fractions)}
         else:
             self.recv = torch.empty(numel, device=self.device, dtype=torch.float16)
         self.flops_total = sum(L * self.flops_fn(r, c) for L, r, c in self.bank_shapes)
@@ -243,6 +296,13 @@ class ShardedOrthogonalizer:
             shapes = [(c, self.bank_shapes[g][1], self.bank_shapes[g][2]) for g, _, c in plan["pieces"]]
             for r, load in enumerate(plan_loads(shapes, plan["slices"], self.flops_fn)):
                 self.flops_per_rank[r] += load
+
+    def _push_fits(self):
+        """Whether every rank's share fits one whole-circuit launch (at most 8
+        problems: one per bank with matrices on the rank, all unpadded)."""
+        if len(self.bank_shapes) > 8:
+            return False
+        return all(r % 8 == 0 and c % 8 == 0 for _, r, c in self.bank_shapes)
 
     def _region(self, plan):
         return self.recv[plan["offset"]:plan["offset"] + self.world_size * plan["seg"]]
@@ -276,7 +336,7 @@ class ShardedOrthogonalizer:
             if tuple(X.shape) != shape:
                 raise ValueError(f"bank shape {tuple(X.shape)} does not match the plan {shape}")
 
-    def _compute_bucket(self, banks, plan):
+    def _compute_bucket(self, banks, plan, push=None):
         ready = getattr(self, "_input_events", None)
         if ready is not None:  # inputs of this bucket still arriving from the host
             torch.cuda.current_stream(self.device).wait_event(ready[id(plan)])
@@ -285,7 +345,10 @@ class ShardedOrthogonalizer:
             inputs.append(banks[g][start:start + view.shape[0]])
             outputs.append(view)
         if inputs:
-            self.grouped_fn(inputs, outputs)
+            if push is not None:
+                self.polar.grouped(inputs, outs=outputs, push=push)
+            else:
+                self.grouped_fn(inputs, outputs)
 
     def compute_local(self, banks):
         """Orthogonalize this rank's slices into its segments (no communication)."""
@@ -307,6 +370,8 @@ class ShardedOrthogonalizer:
         try:
             if self.transport == "copy_engine":
                 self._step_copy_engine(banks)
+            elif self.transport == "push":
+                self._step_push(banks)
             else:
                 self._step_collective(banks)
         finally:
@@ -354,6 +419,36 @@ class ShardedOrthogonalizer:
                     self._peer_recv[p][base:base + plan["seg"]].copy_(src, non_blocking=True)
         self._barrier_on(comm)
         main.wait_stream(comm)
+
+    def _step_push(self, banks):
+        """One launch per rank computes its matrices and stores every result
+        tile into every peer's receive buffer as it is computed. A barrier on
+        the current stream before the launch (no peer still reads the
+        previous step's results) and one after it (every peer's launch, and
+        so every store into this rank's buffer, has completed) order it."""
+        from . import _native
+        main = torch.cuda.current_stream(self.device)
+        plan = self.plans[0]
+        self._barrier_on(main)
+        if not self._push_unsupported:
+            try:
+                self._compute_bucket(banks, plan, push=self._push)
+            except _native.NativeError as e:
+                # Refused before anything ran (shapes or table outside one
+                # whole-circuit launch; the same on every rank): from now on
+                # compute, then copy the segment to the peers. The collective
+                # steps stay the same on every rank.
+                if e.code != _native.PS_ERR_UNSUPPORTED:
+                    raise
+                self._push_unsupported = True
+        if self._push_unsupported:
+            self._compute_bucket(banks, plan)
+            base = plan["offset"] + self.rank * plan["seg"]
+            src = self.recv[base:base + plan["seg"]]
+            for p in range(self.world_size):
+                if p != self.rank:
+                    self._peer_recv[p][base:base + plan["seg"]].copy_(src, non_blocking=True)
+        self._barrier_on(main)
 
     def step_host(self, host_banks, host_out=None):
         """One step from host memory: copies this rank's slices of `host_banks`
@@ -607,6 +702,36 @@ class SplitOrthogonalizer:
                 mats.append(torch.cat(pieces, dim=0 if rows > cols else 1))
             out.append(torch.stack(mats))
         return out
+
+    def _step_push(self, banks):
+        """One launch per rank computes its matrices and stores every result
+        tile into every peer's receive buffer as it is computed. A barrier on
+        the current stream before the launch (no peer still reads the
+        previous step's results) and one after it (every peer's launch, and
+        so every store into this rank's buffer, has completed) order it."""
+        from . import _native
+        main = torch.cuda.current_stream(self.device)
+        plan = self.plans[0]
+        self._barrier_on(main)
+        if not self._push_unsupported:
+            try:
+                self._compute_bucket(banks, plan, push=self._push)
+            except _native.NativeError as e:
+                # Refused before anything ran (shapes or table outside one
+                # whole-circuit launch; the same on every rank): from now on
+                # compute, then copy the segment to the peers. The collective
+                # steps stay the same on every rank.
+                if e.code != _native.PS_ERR_UNSUPPORTED:
+                    raise
+                self._push_unsupported = True
+        if self._push_unsupported:
+            self._compute_bucket(banks, plan)
+            base = plan["offset"] + self.rank * plan["seg"]
+            src = self.recv[base:base + plan["seg"]]
+            for p in range(self.world_size):
+                if p != self.rank:
+                    self._peer_recv[p][base:base + plan["seg"]].copy_(src, non_blocking=True)
+        self._barrier_on(main)
 
     def step_host(self, host_banks, host_out=None):
         """One step from pinned host banks: uploads this rank's matrix, computes

@@ -109,3 +109,75 @@ def test_more_problems_than_one_launch_fall_back(cuda_device):
     on, off = _both(lambda: polar.grouped(banks))
     for a, b in zip(on, off):
         assert torch.equal(a, b)
+
+
+def _packed_outputs(shapes, device, pad=128):
+    """FP16 outputs packed into one buffer (each start 256-byte aligned), as a
+    sharded step's receive segment holds them; returns (buffer, views)."""
+    sizes = [L * r * c for L, r, c in shapes]
+    offs, off = [], 0
+    for n in sizes:
+        offs.append(off)
+        off += -(-n // pad) * pad
+    buf = torch.full((off,), float("nan"), dtype=torch.float16, device=device)
+    views = [buf[o:o + n].view(*s) for o, n, s in zip(offs, sizes, shapes)]
+    return buf, views
+
+
+PUSH_CASES = [
+    ("PS2_55", [(4, 2048, 1024), (7, 1024, 1024), (4, 1024, 2048), (7, 3072, 1024), (4, 1024, 3072)],
+     [1.0, 1.0, 1.0]),
+    ("PS3_55", [(6, 768, 768), (2, 768, 3072), (2, 3072, 768)], [1.0, 2.0]),
+    ("PS2_55", [(5, 256, 512), (3, 128, 128), (2, 136, 200)], [1.0]),
+]
+
+
+@pytest.mark.parametrize("method,shapes,phases", PUSH_CASES,
+                         ids=[f"{m}-{len(s)}-{len(p)}" for m, s, p in PUSH_CASES])
+def test_push_stores_results_into_peer_buffers(cuda_device, method, shapes, phases):
+    """ps_circuit_grouped_push on one GPU, with other buffers of this GPU in
+    place of the peers' copies: the local outputs equal ps_circuit_grouped's
+    bit for bit (phased schedule included), and every 'peer' buffer holds the
+    same bits at the same offsets (nothing outside the outputs written)."""
+    from polar_switch.distributed import phase_ends
+    banks = _banks(shapes, 26, torch.float32, cuda_device)
+    polar = make_polynomial_orthogonalizer(method)
+    want = [y.half() if y.dtype != torch.float16 else y
+            for y in polar.grouped(banks, outs=[torch.empty(b.shape, dtype=torch.float16,
+                                                            device=cuda_device) for b in banks])]
+    local, outs = _packed_outputs(shapes, cuda_device)
+    peers = [torch.full_like(local, float("nan")) for _ in range(3)]
+    push = {"local": local.data_ptr(), "peers": [p.data_ptr() for p in peers],
+            "phase_ends": phase_ends([s[0] for s in shapes], phases)}
+    for _ in range(2):  # a second call over the same buffers
+        polar.grouped(banks, outs=outs, push=push)
+    torch.cuda.synchronize()
+    assert nat.get_status() == 0
+    for o, w, s in zip(outs, want, shapes):
+        assert torch.equal(o, w), f"{method} {s}: pushed launch differs from ps_circuit_grouped"
+    for p in peers:
+        assert torch.equal(torch.isnan(p), torch.isnan(local))
+        m = ~torch.isnan(local)
+        assert torch.equal(p[m], local[m])
+
+
+def test_push_refuses_what_one_launch_cannot_hold(cuda_device):
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    # padded shape: the final apply would go through the workspace
+    X = seeded((2, 130, 66), 27).to(cuda_device)
+    local = torch.empty(2 * 130 * 66 + 128, dtype=torch.float16, device=cuda_device)
+    out = local[:2 * 130 * 66].view(2, 130, 66)
+    push = {"local": local.data_ptr(), "peers": [torch.empty_like(local).data_ptr()],
+            "phase_ends": [[2]]}
+    with pytest.raises(nat.NativeError) as e:
+        polar.grouped([X], outs=[out], push=push)
+    assert e.value.code == nat.PS_ERR_UNSUPPORTED
+    # the whole-circuit kernel switched off
+    prev = nat.set_circuit_kernel(0)
+    try:
+        Y = seeded((2, 128, 64), 28).to(cuda_device)
+        with pytest.raises(nat.NativeError) as e:
+            polar.grouped([Y], outs=[local[:2 * 128 * 64].view(2, 128, 64)], push=push)
+        assert e.value.code == nat.PS_ERR_UNSUPPORTED
+    finally:
+        nat.set_circuit_kernel(prev)

@@ -1,5 +1,6 @@
-"""The sharded Muon step on 2 GPUs (one process per GPU, NCCL): both gather
-transports (copy-engine pushes into symmetric memory, and the NCCL
+"""The sharded Muon step on 2 GPUs (one process per GPU, NCCL): every gather
+transport (result tiles stored into the peer's symmetric memory from inside
+the circuit's launch, copy-engine pushes into symmetric memory, and the NCCL
 all-gather) must give every rank exactly the updates a single process
 computes for the same banks; a matrix split across the two GPUs must stay
 within the circuit's tolerance; and the whole bank-sharded optimizer step
@@ -62,14 +63,17 @@ def _worker(rank, world, port, transport, buckets, q, graph=False):
         step.close()
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, step.transport, [torch.equal(a, b) for a, b in zip(got, want)]))
+        used = step.transport + ("-fallback" if getattr(step, "_push_unsupported", False) else "")
+        q.put((rank, used, [torch.equal(a, b) for a, b in zip(got, want)]))
     except Exception as e:
         q.put((rank, None, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
 
 
 @pytest.mark.parametrize("transport,buckets,graph", [("copy_engine", None, False), ("copy_engine", 3, False),
                                                      ("collective", 2, False), ("copy_engine", 2, True),
-                                                     ("copy_engine", 2, "host")])
+                                                     ("copy_engine", 2, "host"), ("push", None, False),
+                                                     ("push", 3, False), ("push", None, True),
+                                                     ("push", 2, "host")])
 def test_two_gpu_step_matches_single_process(cuda_device, transport, buckets, graph):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

@@ -126,3 +126,38 @@ def test_circuit_kernel_knob_without_gpu():
     prev = lib.ps_set_circuit_kernel(1)
     assert prev in (0, 1)
     assert lib.ps_set_circuit_kernel(prev) == 1
+
+
+def test_push_arguments_without_gpu():
+    """ps_circuit_grouped_push rejects bad peer lists and phase tables before
+    touching a device."""
+    lib = _native.load()
+    null = ctypes.c_void_p(0)
+    ws = ctypes.c_void_p(256)
+    probs = (_native.PsProblem * 2)(
+        _native.PsProblem(256, _native.PS_F32, 4, 256, 128, 256 * 128, 128, 1, 512, _native.PS_F16),
+        _native.PsProblem(256, _native.PS_F32, 3, 128, 128, 128 * 128, 128, 1, 1024, _native.PS_F16))
+    res = (ctypes.c_float * 1)(0.0)
+    nst = (ctypes.c_int32 * 1)(1)
+    steps = (_native.PsStep * 1)(_native.PsStep(1, 0, 0, 1.0, 0.0, 0.0))
+    peers = (ctypes.c_void_p * 8)(*([4096] * 8))
+
+    def call(n_peers, n_phases, ends, peer_list=peers, local=ws):
+        return lib.ps_circuit_grouped_push(probs, 2, 1, res, nst, steps, 2, 1e-7, ws, 1 << 20, local,
+                                           peer_list, n_peers, n_phases, ends, null)
+
+    assert call(8, 1, None) == _native.PS_ERR_INVALID
+    assert b"n_peers" in lib.ps_last_error()
+    assert call(-1, 1, None) == _native.PS_ERR_INVALID
+    assert call(1, 1, None, local=null) == _native.PS_ERR_INVALID
+    odd = (ctypes.c_void_p * 1)(4097)
+    assert call(1, 1, None, peer_list=odd) == _native.PS_ERR_INVALID
+    assert b"misaligned" in lib.ps_last_error()
+    assert call(1, 0, None) == _native.PS_ERR_INVALID
+    assert call(1, 9, None) == _native.PS_ERR_INVALID
+    assert call(1, 2, None) == _native.PS_ERR_INVALID
+    bad_end = (ctypes.c_int32 * 4)(2, 3, 1, 3)   # problem 0 ends at 3, not its L = 4
+    assert call(1, 2, bad_end) == _native.PS_ERR_INVALID
+    assert b"phase_ends" in lib.ps_last_error()
+    decreasing = (ctypes.c_int32 * 4)(3, 4, 2, 1)
+    assert call(1, 2, decreasing) == _native.PS_ERR_INVALID
