@@ -197,6 +197,38 @@ def test_auto_buckets_follow_the_model():
         assert t >= gather and t >= compute + BUCKET_OVERHEAD_S
 
 
+@pytest.mark.parametrize("counts,fractions", [([4, 7, 4, 7, 4], [1, 1, 1]), ([1, 0, 3], [1, 2]),
+                                               ([28, 56], [1.0]), ([5, 2], [1, 2, 4, 8])])
+def test_push_phase_ends(counts, fractions):
+    """Cumulative per-phase counts: one list per input, as many entries as
+    phases, non-decreasing, ending at the input's count, each phase about its
+    fraction of the input."""
+    from polar_switch.distributed import phase_ends
+    ends = phase_ends(counts, fractions)
+    assert len(ends) == len(counts)
+    total = sum(fractions)
+    for c, e in zip(counts, ends):
+        assert len(e) == len(fractions) and e[-1] == c
+        assert all(0 <= a <= b for a, b in zip([0] + e, e))
+        acc = 0.0
+        for f, v in zip(fractions, e):
+            acc += f
+            assert abs(v - c * acc / total) <= 1.0
+
+
+def test_push_is_chosen_only_where_it_can_run():
+    """transport="auto" picks the fused push only for a native CUDA circuit on
+    more than one rank; the gloo tests' CPU ranks take the collective."""
+    from polar_switch.distributed import push_phase_fractions
+    assert push_phase_fractions(2) == [1.0] and len(push_phase_fractions(8)) == 3
+    step = ShardedOrthogonalizer([(4, 64, 32)], device=torch.device("cpu"), world_size=1, rank=0,
+                                 grouped_fn=lambda i, o: None)
+    assert step.transport == "none"
+    with pytest.raises(ValueError):
+        ShardedOrthogonalizer([(4, 64, 32)], device=torch.device("cpu"), world_size=1, rank=0,
+                              grouped_fn=lambda i, o: None, transport="bogus")
+
+
 class _OracleSplitOps:
     """CPU stand-ins for the split-matrix kernels (test infrastructure)."""
 
