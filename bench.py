@@ -683,9 +683,11 @@ def main():
         }
         if single is not None:
             line["single_8192"] = single
-        line["config"]["cuda_graph"] = bool(args.graph)
+        # how the step ran (kept out of `config`, which names the workload and
+        # matches the reference arm's)
+        line["run"] = {"cuda_graph": bool(args.graph)}
         if world > 1:
-            line["config"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
+            line["run"]["gather"] = {"transport": step.transport, "buckets": len(step.plans),
                                         "phases": getattr(step, "phase_fractions", None),
                                         "split_matrices": type(step).__name__ == "SplitOrthogonalizer",
                                         "gemm_ctas": args.gemm_ctas,
