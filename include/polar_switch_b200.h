@@ -307,8 +307,9 @@ PS_API int ps_circuit_grouped_update(const ps_problem* probs, const ps_update* u
  * Every y lies inside one buffer that starts at local_base on this GPU and
  * whose copy on peer k (the same layout) starts at peer_bases[k], a device
  * address this GPU can store to (a peer's symmetric-memory buffer); each
- * final tile is stored to y and to peer_bases[k] + (y - local_base) for k <
- * n_peers (at most 7). The stores are complete when the kernel has finished;
+ * final tile is stored to y and, with 16-byte vector stores, to
+ * peer_bases[k] + (y - local_base) for k < n_peers (at most 7). The stores
+ * are complete when the kernel has finished;
  * ordering them against the peers' use of their buffers (a barrier before and
  * after the call) is the caller's. n_phases (1..8) groups each problem's
  * matrices: phase_ends[i * n_phases + k] is the number of problem i's matrices

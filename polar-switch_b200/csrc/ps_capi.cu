@@ -1529,14 +1529,7 @@ int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const p
     c.y_out = q.y_dtype == PS_F32 ? ps::kOutF32 : q.y_dtype == PS_BF16 ? ps::kOutBF16 : ps::kOutF16;
     if (direct[i] && !upd) {
       if ((rc = map_out(&c.yo, q.y, q.y_dtype, q.cols, q.rows, L, q.cols, q.rows * q.cols))) return rc;
-      if (push)
-        for (int k = 0; k < push->n_peers; ++k) {
-          const uint8_t* peer_y = static_cast<const uint8_t*>(push->peer_bases[k]) +
-                                  (static_cast<const uint8_t*>(q.y) - push->local_base);
-          if ((rc = map_out(&P.ypeer[i][k], peer_y, q.y_dtype, q.cols, q.rows, L, q.cols,
-                            q.rows * q.cols)))
-            return rc;
-        }
+      c.y = static_cast<unsigned char*>(q.y);
     }
     if (upd) {
       c.upd = 1;
@@ -1618,7 +1611,12 @@ int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const p
         }
       }
   }
-  if (push) P.n_peers = push->n_peers;
+  if (push) {
+    P.n_peers = push->n_peers;
+    for (int k = 0; k < push->n_peers; ++k)
+      P.peer_delta[k] = static_cast<long long>(reinterpret_cast<uintptr_t>(push->peer_bases[k]) -
+                                               reinterpret_cast<uintptr_t>(push->local_base));
+  }
   if (tiles > INT32_MAX) return fail(PS_ERR_UNSUPPORTED, "circuit kernel: too many tiles");
   P.item_start[items] = static_cast<int>(tiles);
   P.n_items = items;

@@ -53,6 +53,7 @@ struct alignas(64) CProblem {
   int y_out;                      // kOutF16 / kOutF32 / kOutBF16
   int upd, p_dtype;               // Muon update of P in place of storing y
   void* P;
+  unsigned char* y;               // y (push: the local copy the peers' copies mirror)
   float decay, upd_alpha;
 };
 
@@ -73,12 +74,13 @@ struct alignas(64) CircuitParams {
   int item_start[MAX_ITEMS + 1];
   unsigned short item_first[MAX_ITEMS];  // first matrix (within its problem) of the item's chunk
   unsigned char item_stage[MAX_ITEMS], item_prob[MAX_ITEMS];
-  // Push: every tile a final apply stores into y is also stored, through
-  // ypeer[p][k] (y's layout at another GPU's address), into n_peers other
-  // GPUs' memory. A final apply has no dependent stage, so pushed tiles are
+  // Push: every tile a final apply stores into y is also stored into n_peers
+  // other GPUs' copies of y, at y + peer_delta[k] bytes (plain vector stores
+  // of whole 16-byte granules, eight 64- or 128-byte row segments per warp
+  // instruction). A final apply has no dependent stage, so pushed tiles are
   // not published on the counters; their stores complete by kernel exit.
   int n_peers;
-  CUtensorMap ypeer[MAXP][MAX_PEERS];
+  long long peer_delta[MAX_PEERS];
 };
 static_assert(sizeof(CircuitParams) <= 32764, "kernel parameter space");
 
@@ -206,6 +208,40 @@ __device__ __forceinline__ void stage_row(uint32_t sb, int lane, const float (&f
     for (int j = 0; j < 8; ++j) {
       const int p = j ^ (lane & 7);
       st_shared_v4(sb + lane * 128 + p * 16, w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    }
+  }
+}
+
+// The staged 32-row box (stage_row's layout) stored into every peer's copy
+// of y with 16-byte stores: lane l reads granule l % G of row l / G (G
+// granules per row), so one warp instruction writes 32 / G whole row
+// segments; the registers are reused for every peer. Rows at or beyond M and
+// granules at or beyond N (a multiple of 8 columns) are skipped.
+__device__ __noinline__ void push_box(const CircuitParams& P, unsigned char* y, int out,
+                                         uint32_t sb, int lane, int b, int row0, int gcol0, int M,
+                                         int N) {
+  const int eb = out == kOutF32 ? 4 : 2;           // element bytes
+  const int G = eb == 4 ? 8 : 4;                   // 16-byte granules per staged row
+  const int rows_per = 32 / G;
+  const int j = lane % G;
+  const int col = gcol0 + j * (16 / eb);
+#pragma unroll 1
+  for (int r0 = 0; r0 < 32; r0 += rows_per) {
+    const int r = r0 + lane / G;
+    const int p = eb == 4 ? (j ^ (r & 7)) : (j ^ ((r >> 1) & 3));
+    uint32_t a, bb, c, dd;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(a), "=r"(bb), "=r"(c), "=r"(dd)
+                 : "r"(sb + r * (G * 16) + p * 16));
+    const int row = row0 + r;
+    if (row < M && col < N) {
+      const long long off = ((static_cast<long long>(b) * M + row) * N + col) * eb;
+      for (int k = 0; k < P.n_peers; ++k) {
+        unsigned char* dst = y + off + P.peer_delta[k];
+        asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(a), "r"(bb), "r"(c),
+                     "r"(dd)
+                     : "memory");
+      }
     }
   }
 }
@@ -561,11 +597,10 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
         if (lane == 0) {
           if (row0 < M && gcol0 < N) {
             tma_store_3d(tmD, sb, gcol0, row0, d.b);
-            if (push)
-              for (int k = 0; k < P.n_peers; ++k) tma_store_3d(&P.ypeer[d.p][k], sb, gcol0, row0, d.b);
           }
           bulk_commit();
         }
+        if (push) push_box(P, q.y, out, sb, lane, d.b, row0, gcol0, M, N);
         slot = (slot_bytes == 4096) ? 0 : (slot ^ 1);
       };
       auto release = [&]() {
