@@ -162,6 +162,13 @@ def phase_ends(counts, fractions):
 # the NVLink receive time exceeds the circuits and three equal phases put the
 # first results on the links early (modelled on the whole-circuit kernel's
 # schedule and measured on B200).
+# Largest group for which "auto" picks the push transport. The SM-issued
+# stores reach the peers more slowly than the copy engines (Qwen step on B200,
+# push against copy engines: 3.21 vs 3.30 ms at 2 GPUs, where the transfer
+# hides under the circuits; 2.50 vs 2.25 ms at 4 and 2.40 vs 1.98 ms at 8).
+PUSH_MAX_WORLD = 2
+
+
 def push_phase_fractions(world_size):
     return [1.0] if world_size <= 2 else [1.0, 1.0, 1.0]
 
@@ -219,9 +226,9 @@ class ShardedOrthogonalizer:
         apply stores every result tile into every peer's receive buffer as it
         is computed: the gather fused into the circuit; ``buckets`` then
         give the phases the launch schedules one after another, by default
-        `push_phase_fractions`) or "auto" (push on CUDA when the rank's work
-        fits one whole-circuit launch, else copy engines; the collective off
-        CUDA)."""
+        `push_phase_fractions`) or "auto" (push on CUDA for groups of up to
+        PUSH_MAX_WORLD ranks when the rank's work fits one whole-circuit
+        launch, else copy engines; the collective off CUDA)."""
         self.group = group
         if world_size is None:
             world_size = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -237,8 +244,9 @@ class ShardedOrthogonalizer:
         self.bank_shapes = [tuple(int(v) for v in s) for s in bank_shapes]
         if transport not in ("auto", "copy_engine", "collective", "push"):
             raise ValueError(f"unknown transport {transport!r}")
-        if transport == "auto" and world_size > 1 and self.native_circuit and torch.device(
-                device if device is not None else "cuda").type == "cuda" and self._push_fits():
+        if (transport == "auto" and 1 < world_size <= PUSH_MAX_WORLD and self.native_circuit
+                and torch.device(device if device is not None else "cuda").type == "cuda"
+                and self._push_fits()):
             transport = "push"
         self.phase_fractions = None
         if transport == "push":

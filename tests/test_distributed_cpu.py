@@ -220,7 +220,9 @@ def test_push_is_chosen_only_where_it_can_run():
     """transport="auto" picks the fused push only for a native CUDA circuit on
     more than one rank; the gloo tests' CPU ranks take the collective."""
     from polar_switch.distributed import push_phase_fractions
+    from polar_switch.distributed import PUSH_MAX_WORLD
     assert push_phase_fractions(2) == [1.0] and len(push_phase_fractions(8)) == 3
+    assert PUSH_MAX_WORLD >= 2
     step = ShardedOrthogonalizer([(4, 64, 32)], device=torch.device("cpu"), world_size=1, rank=0,
                                  grouped_fn=lambda i, o: None)
     assert step.transport == "none"
