@@ -529,7 +529,7 @@ def main():
                     help="multi-GPU: cap on GEMM CTAs, leaving SMs to the all-gather")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="enqueue every step from the host instead of replaying a CUDA graph of it")
-    ap.add_argument("--transport", default="auto", choices=["auto", "push", "copy_engine", "collective"],
+    ap.add_argument("--transport", default="auto", choices=["auto", "push", "overlap", "copy_engine", "collective"],
                     help="multi-GPU: result tiles stored into the peers' symmetric memory from inside "
                          "the circuit launch (push; auto when it fits), copy-engine pushes into "
                          "symmetric memory, or the NCCL all-gather")

@@ -327,6 +327,31 @@ PS_API int ps_circuit_grouped_push(const ps_problem* probs, int n_probs, int n_o
                                    const void* const* peer_bases, int n_peers, int n_phases,
                                    const int32_t* phase_ends, void* stream);
 
+/* ps_circuit_grouped in one whole-circuit launch, scheduled in phases like
+ * ps_circuit_grouped_push, that raises a flag in device memory as soon as
+ * every final result of a phase is stored: signals[k] becomes 1 (k <
+ * n_phases) -- for another stream to start moving that phase's results
+ * (copy engines: ps_stream_wait_flag, then peer copies) while the launch
+ * computes the next phases, the all-gather of train_nanogpt.py:4025-4037
+ * overlapping the circuit without splitting it into launches.
+ * signals: PS_SIGNAL_WORDS(n_phases) 32-bit words of device memory, 16-byte
+ * aligned, ZEROED BY THE CALLER before the launch in an order the waiting
+ * stream observes (the words after the flags are the kernel's counters). The
+ * last CTA to finish raises every flag, so a wait on them ends even if the
+ * launch gave up early (ps_get_status then reports why). The bits stored are
+ * ps_circuit_grouped's; same requirements as ps_circuit_grouped_push. */
+#define PS_SIGNAL_WORDS(n_phases) (2 * (n_phases) + 1)
+PS_API int ps_circuit_grouped_signal(const ps_problem* probs, int n_probs, int n_outer,
+                                     const float* residuals, const int32_t* n_steps,
+                                     const ps_step* steps, int buffers, float eps, void* workspace,
+                                     int64_t workspace_bytes, int n_phases,
+                                     const int32_t* phase_ends, unsigned* signals, void* stream);
+
+/* Enqueues on `stream` a wait until the 32-bit word at device address `flag`
+ * is >= value (cuStreamWaitValue32, GEQ); work enqueued after it starts once
+ * the word is written. No counterpart in the reference. */
+PS_API int ps_stream_wait_flag(void* stream, const unsigned* flag, unsigned value);
+
 /* Scratch bytes ps_gns needs for L matrices of rows x cols. */
 PS_API int64_t ps_gns_workspace_bytes(int64_t L, int64_t rows, int64_t cols);
 

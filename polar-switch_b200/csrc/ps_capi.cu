@@ -1428,6 +1428,7 @@ struct CircuitPush {
   int n_peers = 0;
   int n_phases = 1;
   const int32_t* phase_ends = nullptr;
+  unsigned* sig = nullptr;  // phase flags, counters and exit count (see CircuitParams)
 };
 
 // All stages of a grouped circuit in one launch (ps_circuit.cuh). `cur0` is
@@ -1603,13 +1604,20 @@ int circuit_kernel_run(const GroupedPlan& plan, const ps_problem* probs, const p
           P.item_stage[items] = static_cast<unsigned char>(sg);
           P.item_prob[items] = static_cast<unsigned char>(i);
           P.item_first[items] = static_cast<unsigned short>(first);
+          P.item_phase[items] = static_cast<unsigned char>(k);
           ++items;
           const int64_t size = std::min<int64_t>(C[i], b1 - first);
           const int per = P.st_kind[sg] == ps::circ::kApply ? P.prob[i].tiles_m2 * P.prob[i].tiles_n
                                                             : P.prob[i].Tsym;
           tiles += size * per;
+          if (sg == ns - 1)
+            P.sig_target[k] += static_cast<unsigned>(size * per * ps::circ::SIGNALS_PER_TILE);
         }
       }
+  }
+  if (push && push->sig) {
+    P.sig = push->sig;
+    P.n_sig = n_phases;
   }
   if (push) {
     P.n_peers = push->n_peers;
@@ -2188,6 +2196,59 @@ int ps_circuit_grouped_push(const ps_problem* probs, int n_probs, int n_outer, c
                               eps, workspace, workspace_bytes, stream, &push);
 }
 
+int ps_circuit_grouped_signal(const ps_problem* probs, int n_probs, int n_outer,
+                              const float* residuals, const int32_t* n_steps, const ps_step* steps,
+                              int buffers, float eps, void* workspace, int64_t workspace_bytes,
+                              int n_phases, const int32_t* phase_ends, unsigned* signals,
+                              void* stream) {
+  if (!signals || !aligned16(signals))
+    return fail(PS_ERR_INVALID, "ps_circuit_grouped_signal: signals must be 16-byte aligned device memory");
+  if (n_phases < 1 || n_phases > ps::circ::MAX_PHASES)
+    return fail(PS_ERR_INVALID, "ps_circuit_grouped_signal: n_phases must be in [1, %d]",
+                ps::circ::MAX_PHASES);
+  if (!probs || n_probs <= 0) return fail(PS_ERR_INVALID, "ps_circuit: bad problem list");
+  if (n_phases > 1) {
+    if (!phase_ends) return fail(PS_ERR_INVALID, "ps_circuit_grouped_signal: null phase_ends");
+    for (int i = 0; i < n_probs; ++i) {
+      int32_t prev = 0;
+      for (int k = 0; k < n_phases; ++k) {
+        const int32_t e = phase_ends[i * n_phases + k];
+        if (e < prev || (k == n_phases - 1 && e != probs[i].L))
+          return fail(PS_ERR_INVALID,
+                      "ps_circuit_grouped_signal: phase_ends of problem %d must be non-decreasing "
+                      "and end at its L", i);
+        prev = e;
+      }
+    }
+  }
+  CircuitPush push;
+  push.n_phases = n_phases;
+  push.phase_ends = n_phases > 1 ? phase_ends : nullptr;
+  push.sig = signals;
+  return circuit_grouped_impl(probs, nullptr, n_probs, n_outer, residuals, n_steps, steps, buffers,
+                              eps, workspace, workspace_bytes, stream, &push);
+}
+
+int ps_stream_wait_flag(void* stream, const unsigned* flag, unsigned value) {
+  static PFN_cuStreamWaitValue32_v11070 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuStreamWaitValue32", &p, 11070, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuStreamWaitValue32_v11070>(p);
+  });
+  if (!flag || reinterpret_cast<uintptr_t>(flag) % 4)
+    return fail(PS_ERR_INVALID, "ps_stream_wait_flag: flag must be a 4-byte aligned device address");
+  if (!fn) return fail(PS_ERR_CUDA, "cuStreamWaitValue32 entry point unavailable");
+  CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag), value,
+                  CU_STREAM_WAIT_VALUE_GEQ);
+  if (r != CUDA_SUCCESS) return fail(PS_ERR_CUDA, "cuStreamWaitValue32 failed (%d)", static_cast<int>(r));
+  return PS_OK;
+}
+
 static int circuit_grouped_impl(const ps_problem* probs, const ps_update* updates, int n_probs,
                                 int n_outer, const float* residuals, const int32_t* n_steps,
                                 const ps_step* steps, int buffers, float eps, void* workspace,
@@ -2248,7 +2309,7 @@ static int circuit_grouped_impl(const ps_problem* probs, const ps_update* update
     // Checked before anything is launched, so a caller can take another path.
     if (!use_circuit_kernel(plan, np, n_outer, n_steps, buffers))
       return fail(PS_ERR_UNSUPPORTED,
-                  "ps_circuit_grouped_push: the problems do not fit one whole-circuit launch");
+                  "ps_circuit_grouped_push/_signal: the problems do not fit one whole-circuit launch");
     for (int i = 0; i < np; ++i) {
       const ps_problem& q = probs[i];
       const GroupedPlan::Prob& p = plan.probs[i];
@@ -2256,7 +2317,7 @@ static int circuit_grouped_impl(const ps_problem* probs, const ps_update* update
             p.lay.Rp == q.rows && p.lay.Cp == q.cols && (q.cols * elem_bytes(q.y_dtype)) % 16 == 0 &&
             aligned16(q.y)))
         return fail(PS_ERR_UNSUPPORTED,
-                    "ps_circuit_grouped_push: problem %d needs rows and cols multiples of 8 and a "
+                    "ps_circuit_grouped_push/_signal: problem %d needs rows and cols multiples of 8 and a "
                     "16-byte aligned y with 16-byte rows", i);
       if (push->n_peers > 0 && static_cast<const uint8_t*>(q.y) < push->local_base)
         return fail(PS_ERR_INVALID, "ps_circuit_grouped_push: y of problem %d lies before local_base", i);

@@ -81,11 +81,22 @@ struct alignas(64) CircuitParams {
   // not published on the counters; their stores complete by kernel exit.
   int n_peers;
   long long peer_delta[MAX_PEERS];
+  // Phase signals (copy engines moving each phase's results while later
+  // phases compute): sig[k] (k < n_sig) is set to 1 once every final-apply
+  // tile of phase k is stored (sig[n_sig + k] counts their epilogue warps up
+  // to sig_target[k]); sig[2 * n_sig] counts exiting CTAs, and the last one
+  // sets every flag, so a wait on them always ends (after an abort too).
+  // nullptr: off. The caller zeroes sig before the launch.
+  unsigned* sig;
+  int n_sig;
+  unsigned sig_target[MAX_PHASES];
+  unsigned char item_phase[MAX_ITEMS];
 };
 static_assert(sizeof(CircuitParams) <= 32764, "kernel parameter space");
 
 struct Tile {
   int kind, p, b, t, s;  // stage kind, problem, matrix, outer iteration, step index
+  int ph;                // phase of the tile's item
   int m0, n0;            // this CTA's first row; the pair's first column
   unsigned need;         // counter value the tile's inputs wait for (0: none)
 };
@@ -102,6 +113,7 @@ __device__ __forceinline__ void decode(const CircuitParams& P, int t, uint32_t r
   const int sg = P.item_stage[lo];
   const CProblem& q = P.prob[P.item_prob[lo]];
   d.p = P.item_prob[lo];
+  d.ph = P.item_phase[lo];
   d.kind = P.st_kind[sg];
   d.t = P.st_t[sg];
   d.s = P.st_step[sg];
@@ -653,11 +665,18 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
         }
       }
       // Publish this warp's part of the tile (stores complete and visible);
-      // pushed final tiles have no reader in this launch.
+      // pushed final tiles have no reader in this launch. A final tile of a
+      // signalled launch also counts towards its phase, whose flag the last
+      // of its warps raises (system scope: a copy engine reads the data).
       if (lane == 0 && !push) {
         bulk_wait<0>();
         fence_proxy_async_global();
         red_release_gpu_add_u32(P.done + q.g0 + d.b, 1u);
+        if (final_apply && P.sig) {
+          __threadfence_system();
+          const unsigned prev = atomicAdd(P.sig + P.n_sig + d.ph, 1u);
+          if (prev + 1 == P.sig_target[d.ph]) st_release_sys_u32(P.sig + d.ph, 1u);
+        }
       }
       __syncwarp();
       if (++acc == 2) {
@@ -671,6 +690,11 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (P.sig && threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(P.sig + 2 * P.n_sig, 1u) == gridDim.x - 1)
+      for (int k = 0; k < P.n_sig; ++k) st_release_sys_u32(P.sig + k, 1u);
+  }
   cluster_sync();  // neither CTA leaves while the other may still touch it
   tc_fence_after();
   if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);

@@ -132,7 +132,7 @@ class _Circuit:
         return out
 
 
-    def grouped(self, banks, epsilon, outs=None, updates=None, push=None):
+    def grouped(self, banks, epsilon, outs=None, updates=None, push=None, signal=None):
         """Run the circuit on several tensors of different shapes in one C call.
 
         Tensors that share n = min(rows, cols) have their inner iterations
@@ -156,6 +156,12 @@ class _Circuit:
         (cumulative counts ending at the input's matrix count). Raises
         NativeError (PS_ERR_UNSUPPORTED, before anything ran) when the inputs
         do not fit that launch.
+
+        ``signal``: optional dict ``{"flags": int32 device tensor of
+        2 * phases + 1 words, zeroed by the caller, "phase_ends": [...]}``:
+        one launch scheduled in those phases that sets ``flags[k]`` to 1 once
+        phase k's results are stored (ps_circuit_grouped_signal), for another
+        stream to wait on (``_native.stream_wait_flag``).
         """
         if not banks:
             return []
@@ -197,7 +203,23 @@ class _Circuit:
             if ws_bytes < 0:
                 nat.check("ps_circuit_grouped_workspace_bytes", nat.PS_ERR_INVALID)
             ws = torch.empty(ws_bytes, device=device, dtype=torch.uint8)
-            if push is not None:
+            if signal is not None:
+                if upd is not None or push is not None:
+                    raise ValueError("signal cannot be combined with push or updates")
+                ends = signal.get("phase_ends")
+                n_phases = len(ends[0]) if ends else 1
+                if ends and any(len(e) != n_phases for e in ends):
+                    raise ValueError("every input needs the same number of phases")
+                flags = signal["flags"]
+                if flags.device != device or flags.numel() < 2 * n_phases + 1:
+                    raise ValueError("flags must hold 2 * phases + 1 words on the inputs' device")
+                flat = [int(v) for e in ends for v in e] if ends else []
+                nat.check("ps_circuit_grouped_signal", lib.ps_circuit_grouped_signal(
+                    probs, len(banks), self.n_outer, self.residuals, self.n_steps, self.steps,
+                    self.buffers, float(epsilon), nat.ptr(ws), ws_bytes, n_phases,
+                    (ctypes.c_int32 * max(1, len(flat)))(*flat) if flat else None,
+                    nat.ptr(flags), nat.stream_ptr(device)))
+            elif push is not None:
                 if upd is not None:
                     raise ValueError("push and updates cannot be combined")
                 peers = [int(p) for p in push.get("peers", ())]
@@ -282,14 +304,15 @@ def make_polynomial_orthogonalizer(method, compile=True, epsilon=1e-7):
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
 
-    def grouped(tensors, outs=None, updates=None, push=None):
+    def grouped(tensors, outs=None, updates=None, push=None, signal=None):
         """Orthogonalize a list of tensors of different shapes in one grouped call
         (``updates``: fold Muon's update of a parameter bank into the last apply;
         ``push``: also store the results into other GPUs' buffers from inside
         the circuit's launch; see _Circuit.grouped)."""
         for X in tensors:
             _check_input(X)
-        result = circuit.grouped(list(tensors), epsilon, outs=outs, updates=updates, push=push)
+        result = circuit.grouped(list(tensors), epsilon, outs=outs, updates=updates, push=push,
+                                 signal=signal)
         polar.last_execution = dict(requested=name, effective=name, backend=BACKEND)
         return result
 

@@ -33,7 +33,7 @@ EXPORTED = (
     "ps_set_fused_normalize", "ps_circuit_grouped_update", "ps_set_circuit_kernel",
     "ps_set_max_ctas", "ps_gns_workspace_bytes", "ps_gns", "ps_sumsq", "ps_scale_cast",
     "ps_gram_f32", "ps_muon_direction", "ps_muon_update", "ps_update_stats",
-    "ps_circuit_grouped_push",
+    "ps_circuit_grouped_push", "ps_circuit_grouped_signal", "ps_stream_wait_flag",
 )
 
 
@@ -125,6 +125,10 @@ _SIGNATURES = {
                                  ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep), _int, _f32,
                                  _ptr, _i64, _ptr, ctypes.POINTER(_ptr), _int, _int,
                                  ctypes.POINTER(ctypes.c_int32), _ptr], _int),
+    "ps_circuit_grouped_signal": ([ctypes.POINTER(PsProblem), _int, _int, ctypes.POINTER(_f32),
+                                   ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(PsStep), _int, _f32,
+                                   _ptr, _i64, _int, ctypes.POINTER(ctypes.c_int32), _ptr, _ptr], _int),
+    "ps_stream_wait_flag": ([_ptr, _ptr, ctypes.c_uint], _int),
 }
 
 
@@ -150,6 +154,13 @@ def load():
                 fn.restype = res
             _lib = lib
     return _lib
+
+
+def stream_wait_flag(stream, flag_ptr, value=1):
+    """Make `stream` (a torch CUDA stream) wait until the 32-bit word at device
+    address `flag_ptr` is >= value (ps_stream_wait_flag)."""
+    check("ps_stream_wait_flag", load().ps_stream_wait_flag(ctypes.c_void_p(stream.cuda_stream),
+                                                            ctypes.c_void_p(flag_ptr), value))
 
 
 def check(name, code):

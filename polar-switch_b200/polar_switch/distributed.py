@@ -168,6 +168,9 @@ def phase_ends(counts, fractions):
 # hides under the circuits; 2.50 vs 2.25 ms at 4 and 2.40 vs 1.98 ms at 8).
 PUSH_MAX_WORLD = 2
 
+# Phases of the "overlap" transport's launch (equal shares of each bank).
+OVERLAP_PHASES = 4
+
 
 def push_phase_fractions(world_size):
     return [1.0] if world_size <= 2 else [1.0, 1.0, 1.0]
@@ -242,7 +245,7 @@ class ShardedOrthogonalizer:
         table = self.polar.table
         self.flops_fn = lambda r, c: circuit_flops(table, r, c)
         self.bank_shapes = [tuple(int(v) for v in s) for s in bank_shapes]
-        if transport not in ("auto", "copy_engine", "collective", "push"):
+        if transport not in ("auto", "copy_engine", "collective", "push", "overlap"):
             raise ValueError(f"unknown transport {transport!r}")
         if (transport == "auto" and 1 < world_size <= PUSH_MAX_WORLD and self.native_circuit
                 and torch.device(device if device is not None else "cuda").type == "cuda"
@@ -251,6 +254,10 @@ class ShardedOrthogonalizer:
         self.phase_fractions = None
         if transport == "push":
             self.phase_fractions = (push_phase_fractions(world_size) if buckets is None else
+                                    [1.0] * buckets if isinstance(buckets, int) else list(buckets))
+            buckets = 1
+        elif transport == "overlap":
+            self.phase_fractions = ([1.0] * OVERLAP_PHASES if buckets is None else
                                     [1.0] * buckets if isinstance(buckets, int) else list(buckets))
             buckets = 1
         if buckets is None:
@@ -280,7 +287,7 @@ class ShardedOrthogonalizer:
             transport = "none"
         self.transport = transport
         numel = max(offset, 1)
-        if transport in ("copy_engine", "push"):
+        if transport in ("copy_engine", "push", "overlap"):
             import torch.distributed._symmetric_memory as symm
             self.recv = symm.empty(numel, device=self.device, dtype=torch.float16)
             handle = symm.rendezvous(self.recv, self.group if self.group is not None else dist.group.WORLD)
@@ -289,6 +296,28 @@ class ShardedOrthogonalizer:
             self._comm = torch.cuda.Stream(device=self.device)
             self._flag = torch.zeros(1, device=self.device, dtype=torch.int32)
             self._push_unsupported = False
+            if transport == "overlap":
+                plan = self.plans[0]
+                views = self._segment_views(plan, rank)
+                ends = phase_ends([v.shape[0] for _, _, v in views], self.phase_fractions)
+                self._signal = {"flags": torch.zeros(2 * len(self.phase_fractions) + 1, device=self.device,
+                                                     dtype=torch.int32), "phase_ends": ends}
+                # per phase: element ranges of this rank's segment that it completes
+                self._phase_ranges = [[] for _ in self.phase_fractions]
+                off = 0
+                for (_, _, v), e in zip(views, ends):
+                    per = v.shape[1] * v.shape[2]
+                    lo = 0
+                    for k, hi in enumerate(e):
+                        if hi > lo:
+                            rng = self._phase_ranges[k]
+                            start, n = off + lo * per, (hi - lo) * per
+                            if rng and rng[-1][0] + rng[-1][1] == start:
+                                rng[-1] = (rng[-1][0], rng[-1][1] + n)
+                            else:
+                                rng.append((start, n))
+                        lo = hi
+                    off += v.numel()
             if transport == "push":
                 plan = self.plans[0]
                 counts = [v.shape[0] for _, _, v in self._segment_views(plan, self.rank)]
@@ -344,7 +373,7 @@ class ShardedOrthogonalizer:
             if tuple(X.shape) != shape:
                 raise ValueError(f"bank shape {tuple(X.shape)} does not match the plan {shape}")
 
-    def _compute_bucket(self, banks, plan, push=None):
+    def _compute_bucket(self, banks, plan, push=None, signal=None):
         ready = getattr(self, "_input_events", None)
         if ready is not None:  # inputs of this bucket still arriving from the host
             torch.cuda.current_stream(self.device).wait_event(ready[id(plan)])
@@ -353,7 +382,9 @@ class ShardedOrthogonalizer:
             inputs.append(banks[g][start:start + view.shape[0]])
             outputs.append(view)
         if inputs:
-            if push is not None:
+            if signal is not None:
+                self.polar.grouped(inputs, outs=outputs, signal=signal)
+            elif push is not None:
                 self.polar.grouped(inputs, outs=outputs, push=push)
             else:
                 self.grouped_fn(inputs, outputs)
@@ -380,6 +411,8 @@ class ShardedOrthogonalizer:
                 self._step_copy_engine(banks)
             elif self.transport == "push":
                 self._step_push(banks)
+            elif self.transport == "overlap":
+                self._step_overlap(banks)
             else:
                 self._step_collective(banks)
         finally:
@@ -457,6 +490,50 @@ class ShardedOrthogonalizer:
                 if p != self.rank:
                     self._peer_recv[p][base:base + plan["seg"]].copy_(src, non_blocking=True)
         self._barrier_on(main)
+
+    def _step_overlap(self, banks):
+        """One launch per rank computes its matrices phase by phase and raises a
+        device flag as each phase's results are stored; a side stream waits on
+        each flag (ps_stream_wait_flag) and pushes that phase's part of the
+        segment into every peer's receive buffer with copy-engine copies while
+        the launch computes the next phases. Barriers as in the copy-engine
+        step: before the first push (no peer still reads the previous results)
+        and after the last (every push into this rank's buffer is complete)."""
+        from . import _native
+        main = torch.cuda.current_stream(self.device)
+        comm = self._comm
+        plan = self.plans[0]
+        flags = self._signal["flags"]
+        flags.zero_()                      # before the launch and before the waits
+        comm.wait_stream(main)
+        self._barrier_on(comm)
+        base = plan["offset"] + self.rank * plan["seg"]
+        order = [(self.rank + i) % self.world_size for i in range(1, self.world_size)]
+        if not self._push_unsupported:
+            try:
+                self._compute_bucket(banks, plan, signal=self._signal)
+            except _native.NativeError as e:
+                if e.code != _native.PS_ERR_UNSUPPORTED:
+                    raise
+                self._push_unsupported = True
+        if self._push_unsupported:  # refused before anything ran: compute, then copy it all
+            self._compute_bucket(banks, plan)
+            comm.wait_stream(main)
+            ranges = [[(0, plan["seg"])]]
+        else:
+            ranges = self._phase_ranges
+        with torch.cuda.stream(comm):
+            for k, rng in enumerate(ranges):
+                # a phase with results here was launched: its flag is raised
+                # by the launch at the latest when it exits
+                if rng and not self._push_unsupported:
+                    _native.stream_wait_flag(comm, flags.data_ptr() + 4 * k, 1)
+                for start, n in rng:
+                    src = self.recv[base + start:base + start + n]
+                    for p in order:
+                        self._peer_recv[p][base + start:base + start + n].copy_(src, non_blocking=True)
+        self._barrier_on(comm)
+        main.wait_stream(comm)
 
     def step_host(self, host_banks, host_out=None):
         """One step from host memory: copies this rank's slices of `host_banks`
@@ -740,6 +817,50 @@ class SplitOrthogonalizer:
                 if p != self.rank:
                     self._peer_recv[p][base:base + plan["seg"]].copy_(src, non_blocking=True)
         self._barrier_on(main)
+
+    def _step_overlap(self, banks):
+        """One launch per rank computes its matrices phase by phase and raises a
+        device flag as each phase's results are stored; a side stream waits on
+        each flag (ps_stream_wait_flag) and pushes that phase's part of the
+        segment into every peer's receive buffer with copy-engine copies while
+        the launch computes the next phases. Barriers as in the copy-engine
+        step: before the first push (no peer still reads the previous results)
+        and after the last (every push into this rank's buffer is complete)."""
+        from . import _native
+        main = torch.cuda.current_stream(self.device)
+        comm = self._comm
+        plan = self.plans[0]
+        flags = self._signal["flags"]
+        flags.zero_()                      # before the launch and before the waits
+        comm.wait_stream(main)
+        self._barrier_on(comm)
+        base = plan["offset"] + self.rank * plan["seg"]
+        order = [(self.rank + i) % self.world_size for i in range(1, self.world_size)]
+        if not self._push_unsupported:
+            try:
+                self._compute_bucket(banks, plan, signal=self._signal)
+            except _native.NativeError as e:
+                if e.code != _native.PS_ERR_UNSUPPORTED:
+                    raise
+                self._push_unsupported = True
+        if self._push_unsupported:  # refused before anything ran: compute, then copy it all
+            self._compute_bucket(banks, plan)
+            comm.wait_stream(main)
+            ranges = [[(0, plan["seg"])]]
+        else:
+            ranges = self._phase_ranges
+        with torch.cuda.stream(comm):
+            for k, rng in enumerate(ranges):
+                # a phase with results here was launched: its flag is raised
+                # by the launch at the latest when it exits
+                if rng and not self._push_unsupported:
+                    _native.stream_wait_flag(comm, flags.data_ptr() + 4 * k, 1)
+                for start, n in rng:
+                    src = self.recv[base + start:base + start + n]
+                    for p in order:
+                        self._peer_recv[p][base + start:base + start + n].copy_(src, non_blocking=True)
+        self._barrier_on(comm)
+        main.wait_stream(comm)
 
     def step_host(self, host_banks, host_out=None):
         """One step from pinned host banks: uploads this rank's matrix, computes

@@ -181,3 +181,41 @@ def test_push_refuses_what_one_launch_cannot_hold(cuda_device):
         assert e.value.code == nat.PS_ERR_UNSUPPORTED
     finally:
         nat.set_circuit_kernel(prev)
+
+
+def test_signal_flags_release_a_waiting_stream(cuda_device):
+    """ps_circuit_grouped_signal: outputs equal ps_circuit_grouped's, every
+    phase flag ends at 1 with its counter at the expected count, and a side
+    stream that waits on each flag (ps_stream_wait_flag) and then copies that
+    phase's outputs gets the final values."""
+    from polar_switch.distributed import phase_ends
+    shapes = [(6, 512, 256), (5, 256, 256), (4, 256, 768)]
+    banks = _banks(shapes, 29, torch.float32, cuda_device)
+    polar = make_polynomial_orthogonalizer("PS2_55")
+    want = polar.grouped(banks, outs=[torch.empty(b.shape, dtype=torch.float16, device=cuda_device)
+                                      for b in banks])
+    phases = [1.0, 1.0, 2.0]
+    ends = phase_ends([s[0] for s in shapes], phases)
+    flags = torch.zeros(2 * len(phases) + 1, dtype=torch.int32, device=cuda_device)
+    outs = [torch.full(b.shape, float("nan"), dtype=torch.float16, device=cuda_device) for b in banks]
+    copies = [torch.full_like(o, float("nan")) for o in outs]
+    side = torch.cuda.Stream(device=cuda_device)
+    main = torch.cuda.current_stream(cuda_device)
+    for _ in range(2):
+        flags.zero_()
+        side.wait_stream(main)
+        polar.grouped(banks, outs=outs, signal={"flags": flags, "phase_ends": ends})
+        with torch.cuda.stream(side):
+            for k in range(len(phases)):
+                nat.stream_wait_flag(side, flags.data_ptr() + 4 * k, 1)
+                for o, c, e in zip(outs, copies, ends):
+                    lo = e[k - 1] if k else 0
+                    c[lo:e[k]].copy_(o[lo:e[k]], non_blocking=True)
+        main.wait_stream(side)
+        torch.cuda.synchronize()
+        assert nat.get_status() == 0
+        f = flags.cpu()
+        assert f[:len(phases)].tolist() == [1] * len(phases)
+        assert int(f[-1]) > 0  # every CTA counted itself out
+        for o, c, w in zip(outs, copies, want):
+            assert torch.equal(o, w) and torch.equal(c, w)

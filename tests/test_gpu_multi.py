@@ -1,7 +1,8 @@
 """The sharded Muon step on 2 GPUs (one process per GPU, NCCL): every gather
 transport (result tiles stored into the peer's symmetric memory from inside
-the circuit's launch, copy-engine pushes into symmetric memory, and the NCCL
-all-gather) must give every rank exactly the updates a single process
+the circuit's launch; copy-engine pushes of each phase of one launch, started
+by the flags the launch raises; copy-engine pushes per bucket into symmetric
+memory; and the NCCL all-gather) must give every rank exactly the updates a single process
 computes for the same banks; a matrix split across the two GPUs must stay
 within the circuit's tolerance; and the whole bank-sharded optimizer step
 (ShardedMuon) must give every rank the banks one process computes. Skipped
@@ -73,7 +74,8 @@ def _worker(rank, world, port, transport, buckets, q, graph=False):
                                                      ("collective", 2, False), ("copy_engine", 2, True),
                                                      ("copy_engine", 2, "host"), ("push", None, False),
                                                      ("push", 3, False), ("push", None, True),
-                                                     ("push", 2, "host")])
+                                                     ("push", 2, "host"), ("overlap", None, False),
+                                                     ("overlap", 3, True), ("overlap", 2, "host")])
 def test_two_gpu_step_matches_single_process(cuda_device, transport, buckets, graph):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
