@@ -329,6 +329,19 @@ def run_kernel(args):
         nat.set_circuit_kernel(0)  # per-stage launches: the chain runs the inner iterations
         fn = lambda: polar(X, out=Y)  # noqa: E731
         desc = f"chain (PS2_55 circuits) L={L} n={n}"
+    elif args.kernel in ("muon_direction", "muon_update"):
+        # Muon's elementwise kernels on one bank of the workload (BF16 parameters,
+        # gradients and momentum; the stacked direction in BF16)
+        from polar_switch import muon as pm
+        L, r, c = shapes[args.bank]
+        L = args.L or L
+        grads = [torch.randn(r, c, generator=g, device=device).bfloat16() for _ in range(L)]
+        moms = [torch.zeros(r, c, device=device, dtype=torch.bfloat16) for _ in range(L)]
+        params = [torch.randn(r, c, generator=g, device=device).bfloat16() for _ in range(L)]
+        upd = torch.randn(L, r, c, generator=g, device=device).bfloat16()
+        fn = ((lambda: pm.muon_directions(grads, moms, 0.95, torch.bfloat16))
+              if args.kernel == "muon_direction" else (lambda: pm.muon_update(params, upd, 0.999, -0.01)))
+        desc = f"{args.kernel} L={L} {r}x{c} bf16"
     elif args.kernel in ("square", "sym_product"):
         n = min(shapes[args.bank][1:])
         L = args.L or sum(Lg for Lg, r, c in shapes if min(r, c) == n)
@@ -367,7 +380,8 @@ def run_kernel(args):
         fn()
     prof = nat.profile_read()
     nat.profile_enable(False)
-    kind = {"square": "square", "sym_product": "square", "chain": "square"}.get(args.kernel, args.kernel)
+    kind = {"square": "square", "sym_product": "square", "chain": "square", "muon_direction": "other",
+            "muon_update": "other"}.get(args.kernel, args.kernel)
     v = prof[kind]
     ms = v["ms"] / max(v["launches"], 1)
     print(json.dumps({"kernel": desc, "ms_per_launch": ms, "launches": v["launches"],
@@ -518,7 +532,7 @@ def main():
     ap.add_argument("--no-single", dest="single", action="store_false",
                     help="skip the 8192 x 8192 PS2-55 point timed after the step at N = 1")
     ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize", "chain",
-                                         "circuit"],
+                                         "circuit", "muon_direction", "muon_update"],
                     help="time one kernel class alone (for profiling) instead of the whole step")
     ap.add_argument("--bank", type=int, default=0, help="bank of the workload used by --kernel")
     ap.add_argument("--L", type=int, default=0, help="--kernel: override the number of matrices")
