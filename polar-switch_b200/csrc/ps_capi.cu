@@ -1659,13 +1659,19 @@ int launch_muon_direction(const void* const* grads, void* const* moms, int count
     a.E = E;
     a.mu = mu;
     a.nesterov = nesterov;
-    int64_t gx = (E + ps::NORM_THREADS * 4 - 1) / (ps::NORM_THREADS * 4);
+    TO* o = static_cast<TO*>(out) + static_cast<int64_t>(i0) * E;
+    bool vec = E % 8 == 0 && aligned16(o);
+    for (int i = 0; i < n && vec; ++i) vec = aligned16(a.grad[i]) && aligned16(a.mom[i]);
+    int64_t gx = (E + ps::NORM_THREADS * (vec ? 8 : 4) - 1) / (ps::NORM_THREADS * (vec ? 8 : 4));
     const int64_t cap = (8LL * sms + n - 1) / n;
     if (gx > cap) gx = cap;
     if (gx < 1) gx = 1;
     LaunchScope scope(kProfOther, s, 3.0 * n * E, static_cast<double>(n) * E * (3.0 * sizeof(T) + sizeof(TO)));
-    ps::ps_muon_direction_kernel<T, TO><<<dim3(static_cast<unsigned>(gx), n), ps::NORM_THREADS, 0, s>>>(
-        a, static_cast<TO*>(out) + static_cast<int64_t>(i0) * E);
+    const dim3 grid(static_cast<unsigned>(gx), n);
+    if (vec)
+      ps::ps_muon_direction_kernel<T, TO, 8><<<grid, ps::NORM_THREADS, 0, s>>>(a, o);
+    else
+      ps::ps_muon_direction_kernel<T, TO, 1><<<grid, ps::NORM_THREADS, 0, s>>>(a, o);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "muon direction launch");
   }
@@ -1695,13 +1701,19 @@ int launch_muon_update(void* const* params, int count, int64_t E, float decay, f
     a.E = E;
     a.decay = decay;
     a.alpha = alpha;
-    int64_t gx = (E + ps::NORM_THREADS * 4 - 1) / (ps::NORM_THREADS * 4);
+    const TU* u = static_cast<const TU*>(upd) + static_cast<int64_t>(i0) * E;
+    bool vec = E % 8 == 0 && aligned16(u);
+    for (int i = 0; i < n && vec; ++i) vec = aligned16(a.param[i]);
+    int64_t gx = (E + ps::NORM_THREADS * (vec ? 8 : 4) - 1) / (ps::NORM_THREADS * (vec ? 8 : 4));
     const int64_t cap = (8LL * sms + n - 1) / n;
     if (gx > cap) gx = cap;
     if (gx < 1) gx = 1;
     LaunchScope scope(kProfOther, s, 3.0 * n * E, static_cast<double>(n) * E * (2.0 * sizeof(T) + sizeof(TU)));
-    ps::ps_muon_update_kernel<T, TU><<<dim3(static_cast<unsigned>(gx), n), ps::NORM_THREADS, 0, s>>>(
-        a, static_cast<const TU*>(upd) + static_cast<int64_t>(i0) * E);
+    const dim3 grid(static_cast<unsigned>(gx), n);
+    if (vec)
+      ps::ps_muon_update_kernel<T, TU, 8><<<grid, ps::NORM_THREADS, 0, s>>>(a, u);
+    else
+      ps::ps_muon_update_kernel<T, TU, 1><<<grid, ps::NORM_THREADS, 0, s>>>(a, u);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "muon update launch");
   }

@@ -57,8 +57,33 @@ __device__ __forceinline__ __half from_f32<__half>(float v) {
   return __float2half_rn(v);
 }
 
-// grid (x: blocks over the elements, y: matrices of this launch)
-template <typename T, typename TO>
+// The element-wise kernels below move 8 elements per thread and iteration
+// (load8 of ps_norm.cuh, store8 here: 16-byte accesses, two for FP32) when
+// every pointer is 16-byte aligned and a matrix holds a multiple of 8 elements.
+
+// Stores f (values representable in T) as eight elements of T.
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const T lo = from_f32<T>(f[2 * j]), hi = from_f32<T>(f[2 * j + 1]);
+      unsigned short l, h;
+      memcpy(&l, &lo, 2);
+      memcpy(&h, &hi, 2);
+      w[j] = static_cast<uint32_t>(l) | (static_cast<uint32_t>(h) << 16);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// grid (x: blocks over the elements, y: matrices of this launch); VEC = 8:
+// eight elements per thread and iteration (aligned pointers, E % 8 == 0).
+template <typename T, typename TO, int VEC>
 __global__ void __launch_bounds__(NORM_THREADS)
     ps_muon_direction_kernel(const __grid_constant__ MuonDirectionArgs a, TO* __restrict__ out) {
   const int p = blockIdx.y;
@@ -66,14 +91,32 @@ __global__ void __launch_bounds__(NORM_THREADS)
   T* m = static_cast<T*>(a.mom[p]);
   TO* o = out + static_cast<long long>(p) * a.E;
   const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
-  for (long long e = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < a.E;
-       e += stride) {
-    const float gv = to_f32(g[e]);
-    const float m1 = round_to<T>(__fmul_rn(to_f32(m[e]), a.mu));
-    const float m2 = round_to<T>(__fadd_rn(m1, gv));
-    m[e] = from_f32<T>(m2);
-    const float d = a.nesterov ? round_to<T>(__fmaf_rn(a.mu, m2, gv)) : m2;
-    o[e] = from_f32<TO>(d);
+  const long long first = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x;
+  if constexpr (VEC == 8) {
+    for (long long v = first; v < a.E / 8; v += stride) {
+      float gv[8], mv[8], m2[8], d[8];
+      load8(g + 8 * v, gv);
+      load8(m + 8 * v, mv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float m1 = round_to<T>(__fmul_rn(mv[j], a.mu));
+        m2[j] = round_to<T>(__fadd_rn(m1, gv[j]));
+        d[j] = a.nesterov ? round_to<T>(__fmaf_rn(a.mu, m2[j], gv[j])) : m2[j];
+      }
+      store8(m + 8 * v, m2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d[j] = to_f32(from_f32<TO>(d[j]));
+      store8(o + 8 * v, d);
+    }
+  } else {
+    for (long long e = first; e < a.E; e += stride) {
+      const float gv = to_f32(g[e]);
+      const float m1 = round_to<T>(__fmul_rn(to_f32(m[e]), a.mu));
+      const float m2 = round_to<T>(__fadd_rn(m1, gv));
+      m[e] = from_f32<T>(m2);
+      const float d = a.nesterov ? round_to<T>(__fmaf_rn(a.mu, m2, gv)) : m2;
+      o[e] = from_f32<TO>(d);
+    }
   }
 }
 
@@ -87,18 +130,32 @@ struct MuonUpdateArgs {
   float decay, alpha;
 };
 
-template <typename T, typename TU>
+template <typename T, typename TU, int VEC>
 __global__ void __launch_bounds__(NORM_THREADS)
     ps_muon_update_kernel(const __grid_constant__ MuonUpdateArgs a, const TU* __restrict__ upd) {
   const int p = blockIdx.y;
   T* w = static_cast<T*>(a.param[p]);
   const TU* u = upd + static_cast<long long>(p) * a.E;
   const long long stride = static_cast<long long>(gridDim.x) * NORM_THREADS;
-  for (long long e = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x; e < a.E;
-       e += stride) {
-    const float w1 = round_to<T>(__fmul_rn(to_f32(w[e]), a.decay));
-    const float uv = round_to<T>(to_f32(u[e]));
-    w[e] = from_f32<T>(__fmaf_rn(a.alpha, uv, w1));
+  const long long first = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x;
+  if constexpr (VEC == 8) {
+    for (long long v = first; v < a.E / 8; v += stride) {
+      float wv[8], uv[8], r[8];
+      load8(w + 8 * v, wv);
+      load8(u + 8 * v, uv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float w1 = round_to<T>(__fmul_rn(wv[j], a.decay));
+        r[j] = round_to<T>(__fmaf_rn(a.alpha, round_to<T>(uv[j]), w1));
+      }
+      store8(w + 8 * v, r);
+    }
+  } else {
+    for (long long e = first; e < a.E; e += stride) {
+      const float w1 = round_to<T>(__fmul_rn(to_f32(w[e]), a.decay));
+      const float uv = round_to<T>(to_f32(u[e]));
+      w[e] = from_f32<T>(__fmaf_rn(a.alpha, uv, w1));
+    }
   }
 }
 

@@ -440,15 +440,19 @@ class ShardedOrthogonalizer:
         """Push each finished bucket into every peer's receive buffer from a side
         stream while the next bucket computes on the current stream.
 
-        Ordering: the side stream first waits for the current stream and passes
-        a barrier, so no peer still reads the previous step's results when the
-        first push lands; after the last push a second barrier tells every rank
+        Ordering: a barrier on the current stream before the first circuit, which
+        the side stream waits for, so no peer still reads the previous step's
+        results when the first push lands; after the last push a second
+        barrier (on the side stream) tells every rank
         that all pushes into its buffer are complete, and the current stream
         waits for it."""
         main = torch.cuda.current_stream(self.device)
         comm = self._comm
+        # The first barrier runs on the caller's stream before any circuit:
+        # issued on the side stream, its collective kernel could find every SM
+        # held by the first persistent circuit launch and hold back the pushes.
+        self._barrier_on(main)
         comm.wait_stream(main)
-        self._barrier_on(comm)
         order = [(self.rank + i) % self.world_size for i in range(1, self.world_size)]
         for plan in self.plans:
             self._compute_bucket(banks, plan)
@@ -505,8 +509,10 @@ class ShardedOrthogonalizer:
         plan = self.plans[0]
         flags = self._signal["flags"]
         flags.zero_()                      # before the launch and before the waits
+        # first barrier on the caller's stream, before the persistent launch
+        # takes every SM (on the side stream it would wait for that launch)
+        self._barrier_on(main)
         comm.wait_stream(main)
-        self._barrier_on(comm)
         base = plan["offset"] + self.rank * plan["seg"]
         order = [(self.rank + i) % self.world_size for i in range(1, self.world_size)]
         if not self._push_unsupported:
@@ -832,8 +838,10 @@ class SplitOrthogonalizer:
         plan = self.plans[0]
         flags = self._signal["flags"]
         flags.zero_()                      # before the launch and before the waits
+        # first barrier on the caller's stream, before the persistent launch
+        # takes every SM (on the side stream it would wait for that launch)
+        self._barrier_on(main)
         comm.wait_stream(main)
-        self._barrier_on(comm)
         base = plan["offset"] + self.rank * plan["seg"]
         order = [(self.rank + i) % self.world_size for i in range(1, self.world_size)]
         if not self._push_unsupported:
