@@ -529,6 +529,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=12.0, help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-buckets", type=int, default=32,
+                    help="1 GPU: buckets of the end-to-end host step (copies overlap the circuits bucket by bucket)")
     ap.add_argument("--no-single", dest="single", action="store_false",
                     help="skip the 8192 x 8192 PS2-55 point timed after the step at N = 1")
     ap.add_argument("--kernel", choices=["square", "sym_product", "gram", "apply", "normalize", "chain",
@@ -631,13 +633,13 @@ def main():
     # rank uploads its own slices from pinned memory bucket by bucket, computes
     # each bucket as its inputs land and downloads the full gathered FP16
     # update set, the transfers overlapping the circuits. With one GPU the
-    # host path uses its own plan of 8 buckets (the device-resident step above
+    # host path uses its own plan of --e2e-buckets buckets (the device-resident step above
     # needs none).
     host_banks = [b.cpu().pin_memory() for b in banks]
     host_step = step
     if world == 1:
         host_step = ShardedOrthogonalizer(shapes, method=method, group=None, device=device,
-                                          world_size=1, rank=0, buckets=8)
+                                          world_size=1, rank=0, buckets=args.e2e_buckets)
     host_out = torch.empty(host_step.recv.numel(), dtype=torch.float16).pin_memory()
     ranges = host_step.local_ranges()
     h2d = sum(count * shapes[g][1] * shapes[g][2] * 4 for g, _, count in ranges)
