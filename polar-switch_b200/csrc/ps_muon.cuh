@@ -13,6 +13,8 @@
 // stacked copy several times; here each is touched once.
 #pragma once
 
+#include <type_traits>
+
 #include "ps_norm.cuh"
 
 namespace ps {
@@ -61,6 +63,28 @@ __device__ __forceinline__ __half from_f32<__half>(float v) {
 // (load8 of ps_norm.cuh, store8 here: 16-byte accesses, two for FP32) when
 // every pointer is 16-byte aligned and a matrix holds a multiple of 8 elements.
 
+// Rounds eight FP32 values to T's precision in place (round to nearest
+// even), two per packed convert for the 16-bit types; the same values as
+// round_to<T> on each.
+template <typename T>
+__device__ __forceinline__ void round8(float (&f)[8]) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 g = __bfloat1622float2(__floats2bfloat162_rn(f[2 * j], f[2 * j + 1]));
+      f[2 * j] = g.x;
+      f[2 * j + 1] = g.y;
+    }
+  } else if constexpr (std::is_same<T, __half>::value) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 g = __half22float2(__floats2half2_rn(f[2 * j], f[2 * j + 1]));
+      f[2 * j] = g.x;
+      f[2 * j + 1] = g.y;
+    }
+  }
+}
+
 // Stores f (values representable in T) as eight elements of T.
 template <typename T>
 __device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
@@ -98,14 +122,16 @@ __global__ void __launch_bounds__(NORM_THREADS)
       load8(g + 8 * v, gv);
       load8(m + 8 * v, mv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float m1 = round_to<T>(__fmul_rn(mv[j], a.mu));
-        m2[j] = round_to<T>(__fadd_rn(m1, gv[j]));
-        d[j] = a.nesterov ? round_to<T>(__fmaf_rn(a.mu, m2[j], gv[j])) : m2[j];
-      }
-      store8(m + 8 * v, m2);
+      for (int j = 0; j < 8; ++j) m2[j] = __fmul_rn(mv[j], a.mu);
+      round8<T>(m2);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) d[j] = to_f32(from_f32<TO>(d[j]));
+      for (int j = 0; j < 8; ++j) m2[j] = __fadd_rn(m2[j], gv[j]);
+      round8<T>(m2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d[j] = a.nesterov ? __fmaf_rn(a.mu, m2[j], gv[j]) : m2[j];
+      round8<T>(d);
+      store8(m + 8 * v, m2);
+      round8<TO>(d);
       store8(o + 8 * v, d);
     }
   } else {
@@ -140,15 +166,17 @@ __global__ void __launch_bounds__(NORM_THREADS)
   const long long first = static_cast<long long>(blockIdx.x) * NORM_THREADS + threadIdx.x;
   if constexpr (VEC == 8) {
     for (long long v = first; v < a.E / 8; v += stride) {
-      float wv[8], uv[8], r[8];
+      float wv[8], uv[8];
       load8(w + 8 * v, wv);
       load8(u + 8 * v, uv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float w1 = round_to<T>(__fmul_rn(wv[j], a.decay));
-        r[j] = round_to<T>(__fmaf_rn(a.alpha, round_to<T>(uv[j]), w1));
-      }
-      store8(w + 8 * v, r);
+      for (int j = 0; j < 8; ++j) wv[j] = __fmul_rn(wv[j], a.decay);
+      round8<T>(wv);
+      round8<T>(uv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[j] = __fmaf_rn(a.alpha, uv[j], wv[j]);
+      round8<T>(wv);
+      store8(w + 8 * v, wv);
     }
   } else {
     for (long long e = first; e < a.E; e += stride) {
