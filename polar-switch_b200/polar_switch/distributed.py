@@ -156,6 +156,29 @@ def phase_ends(counts, fractions):
     return out
 
 
+def phase_ranges(shapes, ends):
+    """Per phase, the (start, length) element ranges of a segment that packs
+    inputs of `shapes` ((count, rows, cols) each) one after another, covering
+    the matrices each phase completes (`ends` from phase_ends); adjacent
+    ranges are merged."""
+    out = [[] for _ in (ends[0] if ends else [])]
+    off = 0
+    for (count, rows, cols), e in zip(shapes, ends):
+        per = rows * cols
+        lo = 0
+        for k, hi in enumerate(e):
+            if hi > lo:
+                rng = out[k]
+                start, n = off + lo * per, (hi - lo) * per
+                if rng and rng[-1][0] + rng[-1][1] == start:
+                    rng[-1] = (rng[-1][0], rng[-1][1] + n)
+                else:
+                    rng.append((start, n))
+            lo = hi
+        off += count * per
+    return out
+
+
 # Push transport: phases of the rank's matrices inside its one launch. With
 # two ranks the step is compute-bound (each GPU receives half the updates
 # while computing the other half) and one phase is best; from four ranks on
@@ -308,22 +331,7 @@ class ShardedOrthogonalizer:
                 ends = phase_ends([v.shape[0] for _, _, v in views], self.phase_fractions)
                 self._signal = {"flags": torch.zeros(2 * len(self.phase_fractions) + 1, device=self.device,
                                                      dtype=torch.int32), "phase_ends": ends}
-                # per phase: element ranges of this rank's segment that it completes
-                self._phase_ranges = [[] for _ in self.phase_fractions]
-                off = 0
-                for (_, _, v), e in zip(views, ends):
-                    per = v.shape[1] * v.shape[2]
-                    lo = 0
-                    for k, hi in enumerate(e):
-                        if hi > lo:
-                            rng = self._phase_ranges[k]
-                            start, n = off + lo * per, (hi - lo) * per
-                            if rng and rng[-1][0] + rng[-1][1] == start:
-                                rng[-1] = (rng[-1][0], rng[-1][1] + n)
-                            else:
-                                rng.append((start, n))
-                        lo = hi
-                    off += v.numel()
+                self._phase_ranges = phase_ranges([tuple(v.shape) for _, _, v in views], ends)
             if transport == "push":
                 plan = self.plans[0]
                 counts = [v.shape[0] for _, _, v in self._segment_views(plan, self.rank)]

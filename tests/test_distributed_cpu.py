@@ -216,6 +216,33 @@ def test_push_phase_ends(counts, fractions):
             assert abs(v - c * acc / total) <= 1.0
 
 
+def test_overlap_phase_ranges_cover_each_output_once():
+    """The ranges the overlap transport copies after each phase flag tile the
+    rank's segment exactly: every element once, in the phase that finishes it."""
+    from polar_switch.distributed import phase_ends, phase_ranges
+    shapes = [(4, 16, 8), (7, 8, 8), (1, 24, 16), (0, 8, 8)]
+    shapes = [s for s in shapes if s[0]]
+    for fr in ([1.0], [1, 1, 1], [1, 2, 4, 8]):
+        ends = phase_ends([s[0] for s in shapes], fr)
+        rng = phase_ranges(shapes, ends)
+        assert len(rng) == len(fr)
+        covered = []
+        for k, r in enumerate(rng):
+            for start, n in r:
+                covered.extend(range(start, start + n))
+        assert sorted(covered) == list(range(sum(c * r * q for c, r, q in shapes)))
+        # the matrices of phase k of input i lie in phase k's ranges
+        off = 0
+        for (c, r, q), e in zip(shapes, ends):
+            lo = 0
+            for k, hi in enumerate(e):
+                for m in range(lo, hi):
+                    a = off + m * r * q
+                    assert any(s0 <= a and a + r * q <= s0 + n for s0, n in rng[k])
+                lo = hi
+            off += c * r * q
+
+
 def test_push_is_chosen_only_where_it_can_run():
     """transport="auto" picks the fused push only for a native CUDA circuit on
     more than one rank; the gloo tests' CPU ranks take the collective."""
