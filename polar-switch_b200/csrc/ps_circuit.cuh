@@ -673,8 +673,10 @@ __global__ void __launch_bounds__(pair::NUM_THREADS, 1)
         fence_proxy_async_global();
         red_release_gpu_add_u32(P.done + q.g0 + d.b, 1u);
         if (final_apply && P.sig) {
-          __threadfence_system();
-          const unsigned prev = atomicAdd(P.sig + P.n_sig + d.ph, 1u);
+          // GPU-scope acquire-release count (the stores are complete and
+          // fenced above); the last warp of the phase, having acquired every
+          // other warp's part, raises the flag with a system-scope release.
+          const unsigned prev = atom_acq_rel_gpu_add_u32(P.sig + P.n_sig + d.ph, 1u);
           if (prev + 1 == P.sig_target[d.ph]) st_release_sys_u32(P.sig + d.ph, 1u);
         }
       }
