@@ -408,6 +408,41 @@ PUBLISHED_MS = {
 }
 
 
+def time_other_configs(device, warmup, calls=10):
+    """BASELINE configs 3 and 5 on one GPU, timed alongside the headline: the
+    NanoGPT batch (48 x 768^2 + 12 x 768x3072 + 12 x 3072x768, N(0, 0.02^2))
+    and the Gemma-3-1B step (26 layers), both PS3-55, each one grouped call
+    into FP16 outputs, median of `calls` calls timed alone with CUDA events
+    after a warm-up; FLOPs as the reference counts them."""
+    from polar_switch import circuit_flops, coefficients, make_polynomial_orthogonalizer
+    out = {}
+    for name, scale in (("nanogpt", 0.02), ("gemma", 1.0)):
+        shapes = bank_shapes(name)
+        method = WORKLOADS[name]["method"]
+        banks = make_banks(shapes, device, seed=0, scale=scale)
+        outs = [torch.empty(b.shape, dtype=torch.float16, device=device) for b in banks]
+        polar = make_polynomial_orthogonalizer(method)
+        flops = sum(L * circuit_flops(getattr(coefficients, method), r, c) for L, r, c in shapes)
+        for _ in range(max(warmup, 3)):
+            polar.grouped(banks, outs=outs)
+        torch.cuda.synchronize(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        times = []
+        for _ in range(calls):
+            s.record()
+            polar.grouped(banks, outs=outs)
+            e.record()
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+        times.sort()
+        ms = times[len(times) // 2]
+        out[name] = {"workload": WORKLOADS[name]["desc"], "method": method,
+                     "matrices": sum(L for L, _, _ in shapes), "median_ms": round(ms, 4),
+                     "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "calls": calls}
+        del banks, outs
+    return out
+
+
 def time_single_8192(device, warmup, calls=15):
     """The 8192 x 8192 PS2-55 circuit of the reference's published B200 heatmap
     (7.47 ms median, README.md:77-81), timed call by call with CUDA events on
@@ -666,9 +701,14 @@ def main():
         cpu_baseline = {"value": flops / step_s / 1e12, "unit": "TFLOP/s",
                         "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
 
-    single = None
+    single = others = None
     if world == 1 and args.single and args.workload != "single":
         single = time_single_8192(device, args.warmup)
+    if world == 1 and args.single and args.workload == "qwen":
+        try:
+            others = time_other_configs(device, args.warmup)
+        except Exception as e:  # an auxiliary measurement: report it, keep the headline line
+            others = {"error": f"{type(e).__name__}: {e}"}
 
     if rank == 0:
         peaks = load_peaks()
@@ -699,6 +739,8 @@ def main():
         }
         if single is not None:
             line["single_8192"] = single
+        if others is not None:
+            line["other_configs"] = others
         # how the step ran (kept out of `config`, which names the workload and
         # matches the reference arm's)
         line["run"] = {"cuda_graph": bool(args.graph)}
